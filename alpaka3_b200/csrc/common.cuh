@@ -1,0 +1,181 @@
+// Shared device/host helpers of the alpaka3_b200 CUDA library (sm_100a only).
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <cstdio>
+#include <string>
+
+#include "alpaka3_b200.h"
+
+#if defined(__CUDA_ARCH__) && (__CUDA_ARCH__ < 1000)
+#error "alpaka3_b200 is built for sm_100a (B200) only"
+#endif
+
+namespace a3b
+{
+    // ------------------------------------------------------------------------------------------- host errors
+    void setError(char const* fmt, ...);
+    int cudaFail(cudaError_t e, char const* what);
+
+#define A3B_CUDA(call)                                                                                                \
+    do                                                                                                                \
+    {                                                                                                                 \
+        cudaError_t a3b_e_ = (call);                                                                                  \
+        if(a3b_e_ != cudaSuccess)                                                                                     \
+            return ::a3b::cudaFail(a3b_e_, #call);                                                                    \
+    } while(0)
+
+#define A3B_CHECK_LAUNCH(what)                                                                                        \
+    do                                                                                                                \
+    {                                                                                                                 \
+        cudaError_t a3b_e_ = cudaGetLastError();                                                                      \
+        if(a3b_e_ != cudaSuccess)                                                                                     \
+            return ::a3b::cudaFail(a3b_e_, what);                                                                     \
+    } while(0)
+
+#define A3B_REQUIRE(cond, msg)                                                                                        \
+    do                                                                                                                \
+    {                                                                                                                 \
+        if(!(cond))                                                                                                   \
+        {                                                                                                             \
+            ::a3b::setError("%s", msg);                                                                               \
+            return A3B_ERR_INVALID;                                                                                   \
+        }                                                                                                             \
+    } while(0)
+
+    // -------------------------------------------------------------------------------- per-device properties
+    struct DeviceProps
+    {
+        int ordinal = -1;
+        int smCount = 0;
+        int ccMajor = 0;
+        int ccMinor = 0;
+        size_t l2Bytes = 0;
+        unsigned* errWord = nullptr; // device address of this device's error word
+    };
+
+    // properties of the current device (cached); returns A3B_OK or an error status
+    int currentDevice(DeviceProps const** props);
+
+    // Bounded-wait limit (ns) passed to kernels that spin.
+    uint64_t waitTimeoutNs();
+
+    // Scratch cached per (device, stream, slot): at least `bytes`, zero-filled when first allocated or grown.
+    // Work ordered on `stream` may use it; each slot belongs to one kernel family, which leaves it in the state its
+    // next call expects.
+    enum ScratchSlot
+    {
+        kScratchReduce = 0,
+        kScratchScan = 1,
+        kScratchNbody = 2,
+        kScratchSlots = 3
+    };
+    int streamScratch(cudaStream_t stream, int slot, size_t bytes, void** ptr);
+
+
+    inline int dtypeSize(int dtype)
+    {
+        switch(dtype)
+        {
+        case A3B_I32:
+        case A3B_U32:
+        case A3B_F32:
+            return 4;
+        case A3B_I64:
+        case A3B_U64:
+        case A3B_F64:
+            return 8;
+        default:
+            return 0;
+        }
+    }
+
+    inline bool aligned16(void const* p)
+    {
+        return (reinterpret_cast<uintptr_t>(p) & 15u) == 0u;
+    }
+
+    // ------------------------------------------------------------------------------------------ device side
+    constexpr unsigned kErrTimeout = 1u;
+
+    __device__ __forceinline__ uint64_t globalTimerNs()
+    {
+        uint64_t t;
+        asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+        return t;
+    }
+
+    __device__ __forceinline__ uint64_t ldRelaxedU64(uint64_t const* p)
+    {
+        uint64_t v;
+        asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+        return v;
+    }
+
+    __device__ __forceinline__ void stRelaxedU64(uint64_t* p, uint64_t v)
+    {
+        asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+    }
+
+    __device__ __forceinline__ unsigned ldAcquireU32(unsigned const* p)
+    {
+        unsigned v;
+        asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+        return v;
+    }
+
+    __device__ __forceinline__ void stReleaseU32(unsigned* p, unsigned v)
+    {
+        asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+    }
+
+    __device__ __forceinline__ unsigned ldRelaxedU32(unsigned const* p)
+    {
+        unsigned v;
+        asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+        return v;
+    }
+
+    __device__ __forceinline__ void stRelaxedU32(unsigned* p, unsigned v)
+    {
+        asm volatile("st.relaxed.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+    }
+
+    // streaming 16-byte loads/stores (data touched once: evict-first in L1/L2)
+    template<typename V>
+    __device__ __forceinline__ V ldStream(V const* p)
+    {
+        return __ldcs(p);
+    }
+
+    template<typename V>
+    __device__ __forceinline__ void stStream(V* p, V v)
+    {
+        __stcs(p, v);
+    }
+
+    // ---------------------------------------------------------------------------------------------- Philox
+    // Philox4x32-10 (Salmon et al., SC'11): counter (i_lo, i_hi, 0, 0), key (seed_lo, seed_hi)
+    __host__ __device__ __forceinline__ uint4 philox4x32_10(uint64_t seed, uint64_t i)
+    {
+        uint32_t c0 = static_cast<uint32_t>(i), c1 = static_cast<uint32_t>(i >> 32), c2 = 0u, c3 = 0u;
+        uint32_t k0 = static_cast<uint32_t>(seed), k1 = static_cast<uint32_t>(seed >> 32);
+#pragma unroll
+        for(int r = 0; r < 10; ++r)
+        {
+            uint64_t const p0 = static_cast<uint64_t>(0xD2511F53u) * c0;
+            uint64_t const p1 = static_cast<uint64_t>(0xCD9E8D57u) * c2;
+            uint32_t const n0 = static_cast<uint32_t>(p1 >> 32) ^ c1 ^ k0;
+            uint32_t const n2 = static_cast<uint32_t>(p0 >> 32) ^ c3 ^ k1;
+            c1 = static_cast<uint32_t>(p1);
+            c3 = static_cast<uint32_t>(p0);
+            c0 = n0;
+            c2 = n2;
+            k0 += 0x9E3779B9u;
+            k1 += 0xBB67AE85u;
+        }
+        return make_uint4(c0, c1, c2, c3);
+    }
+} // namespace a3b

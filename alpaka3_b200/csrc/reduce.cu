@@ -1,0 +1,511 @@
+// One-pass transform-reduce: onHost::transformReduce / onHost::reduce and the BabelStream dot.
+//
+// Replaces SimdTransformReduceKernel + its host driver (include/alpaka/onHost/algo/internal/transformReduce.hpp:23-202)
+// and SimdTransformReduce::reduceSimdPackExecution (include/alpaka/onAcc/internal/SimdTransformReduce.hpp:359-499).
+//
+// Design (one launch, no pre-fill of `out`):
+//   * a resident grid (SM count x resident blocks) walks the input in 16-byte packs, UNROLL packs per thread per
+//     iteration, each into its own accumulator (independent dependency chains);
+//   * fp32 inputs: the transformed elements of one pack are summed in fp32, the pack sum is added to an fp64
+//     accumulator; fp64 inputs accumulate in fp64; integer + accumulates in 64-bit unsigned (wraps like the
+//     reference's atomicAdd on the narrow type once truncated);
+//   * warp butterfly (shfl_xor), then a block step through shared memory, gives one partial per block;
+//   * the last block to finish (threadfence + atomic ticket) combines the partials in block order and writes out[0],
+//     then resets the ticket, so the scratch is left ready for the next call on the stream.
+// The result depends only on (device SM count, n): repeated runs give identical bits.
+#include <cfloat>
+#include <climits>
+#include <type_traits>
+
+#include "common.cuh"
+
+namespace a3b
+{
+    namespace
+    {
+        constexpr int kBlock = 256;
+        constexpr int kUnroll = 4;
+        constexpr int kWarps = kBlock / 32;
+
+        // accumulator type
+        template<typename T, int ROp>
+        struct AccOf
+        {
+            using type = std::conditional_t<
+                std::is_floating_point_v<T>,
+                std::conditional_t<ROp == A3B_REDUCE_PLUS, double, T>,
+                std::conditional_t<ROp == A3B_REDUCE_PLUS, uint64_t, T>>;
+        };
+
+        template<typename A, int ROp>
+        __device__ __forceinline__ A combine(A x, A y)
+        {
+            if constexpr(ROp == A3B_REDUCE_PLUS)
+            {
+                if constexpr(std::is_same_v<A, double>)
+                    return __dadd_rn(x, y);
+                else
+                    return x + y;
+            }
+            else if constexpr(ROp == A3B_REDUCE_MIN)
+                return y < x ? y : x;
+            else
+                return y > x ? y : x;
+        }
+
+        template<int XOp, typename T>
+        __device__ __forceinline__ T xform(T x, T y)
+        {
+            if constexpr(XOp == A3B_XFORM_IDENTITY)
+                return x;
+            else if constexpr(XOp == A3B_XFORM_SQUARE)
+            {
+                if constexpr(std::is_same_v<T, float>)
+                    return __fmul_rn(x, x);
+                else if constexpr(std::is_same_v<T, double>)
+                    return __dmul_rn(x, x);
+                else
+                    return static_cast<T>(static_cast<std::make_unsigned_t<T>>(x) * static_cast<std::make_unsigned_t<T>>(x));
+            }
+            else
+            {
+                if constexpr(std::is_same_v<T, float>)
+                    return __fmul_rn(x, y);
+                else if constexpr(std::is_same_v<T, double>)
+                    return __dmul_rn(x, y);
+                else
+                    return static_cast<T>(static_cast<std::make_unsigned_t<T>>(x) * static_cast<std::make_unsigned_t<T>>(y));
+            }
+        }
+
+        // widen one transformed element into the accumulator type
+        template<typename A, typename T>
+        __device__ __forceinline__ A widen(T v)
+        {
+            if constexpr(std::is_same_v<A, uint64_t> && std::is_signed_v<T>)
+                return static_cast<uint64_t>(static_cast<int64_t>(v));
+            else
+                return static_cast<A>(v);
+        }
+
+        template<typename T, int W>
+        struct alignas(16) Pack
+        {
+            T v[W];
+        };
+
+        template<typename T, int W>
+        __device__ __forceinline__ Pack<T, W> loadPack(T const* base, uint64_t packIdx)
+        {
+            if constexpr(W * sizeof(T) == 16)
+            {
+                uint4 raw = __ldcs(reinterpret_cast<uint4 const*>(base) + packIdx);
+                return *reinterpret_cast<Pack<T, W>*>(&raw);
+            }
+            else
+            {
+                Pack<T, W> p;
+#pragma unroll
+                for(int k = 0; k < W; ++k)
+                    p.v[k] = __ldcs(base + packIdx * W + k);
+                return p;
+            }
+        }
+
+        // fold one pack (already transformed element-wise) into an accumulator
+        template<typename T, int W, int ROp, int XOp, typename A>
+        __device__ __forceinline__ A foldPack(A acc, Pack<T, W> const& x, Pack<T, W> const& y)
+        {
+            if constexpr(std::is_same_v<T, float> && ROp == A3B_REDUCE_PLUS)
+            {
+                // fp32 pack sum (pairwise), then one fp64 add
+                float t[W];
+#pragma unroll
+                for(int k = 0; k < W; ++k)
+                    t[k] = xform<XOp>(x.v[k], y.v[k]);
+#pragma unroll
+                for(int w = 1; w < W; w *= 2)
+#pragma unroll
+                    for(int k = 0; k + w < W; k += 2 * w)
+                        t[k] = __fadd_rn(t[k], t[k + w]);
+                return __dadd_rn(acc, static_cast<double>(t[0]));
+            }
+            else
+            {
+#pragma unroll
+                for(int k = 0; k < W; ++k)
+                    acc = combine<A, ROp>(acc, widen<A>(xform<XOp>(x.v[k], y.v[k])));
+                return acc;
+            }
+        }
+
+        template<typename A>
+        __device__ __forceinline__ A shflXor(A v, int m)
+        {
+            return __shfl_xor_sync(0xffffffffu, v, m);
+        }
+
+        template<typename A, int ROp>
+        __device__ __forceinline__ A warpReduce(A v)
+        {
+#pragma unroll
+            for(int m = 16; m > 0; m >>= 1)
+                v = combine<A, ROp>(v, shflXor(v, m));
+            return v;
+        }
+
+        template<typename A, int ROp>
+        __device__ __forceinline__ A blockReduce(A v, A* smem)
+        {
+            v = warpReduce<A, ROp>(v);
+            int const warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+            __syncthreads(); // smem may still be read by a previous blockReduce
+            if(lane == 0)
+                smem[warp] = v;
+            __syncthreads();
+            A r = smem[0];
+#pragma unroll
+            for(int w = 1; w < kWarps; ++w)
+                r = combine<A, ROp>(r, smem[w]);
+            return r;
+        }
+
+        struct ReduceScratch
+        {
+            unsigned ticket;
+            unsigned pad[15];
+        };
+
+        // Finish: convert accumulator to the output element (or store the raw partial).
+        template<typename T, typename A>
+        __device__ __forceinline__ void writeResult(void* out, A r, bool rawPartial)
+        {
+            if(rawPartial)
+            {
+                // 8-byte partial: double for float types, 64-bit integer for integer types
+                if constexpr(std::is_floating_point_v<T>)
+                    *static_cast<double*>(out) = static_cast<double>(r);
+                else if constexpr(std::is_signed_v<T>)
+                    *static_cast<int64_t*>(out) = static_cast<int64_t>(r);
+                else
+                    *static_cast<uint64_t*>(out) = static_cast<uint64_t>(r);
+            }
+            else
+            {
+                if constexpr(std::is_same_v<A, uint64_t> && !std::is_same_v<T, uint64_t>)
+                    *static_cast<T*>(out) = static_cast<T>(static_cast<std::make_unsigned_t<T>>(r));
+                else
+                    *static_cast<T*>(out) = static_cast<T>(r);
+            }
+        }
+
+        // PITCHED: rows of rowLen elements, rowPitch bytes apart; packs never straddle rows (rowLen % W == 0).
+        template<typename T, int W, int ROp, int XOp, bool PITCHED>
+        __global__ void __launch_bounds__(kBlock) reduceKernel(
+            T const* __restrict__ in0,
+            T const* __restrict__ in1,
+            uint64_t n,
+            uint64_t rowLen,
+            uint64_t rowPitch,
+            T neutral,
+            void* out,
+            bool rawPartial,
+            ReduceScratch* scratch,
+            typename AccOf<T, ROp>::type* partials)
+        {
+            using A = typename AccOf<T, ROp>::type;
+            __shared__ A smem[kWarps];
+            __shared__ bool amLast;
+
+            A const neutralA = widen<A>(neutral);
+            A acc[kUnroll];
+#pragma unroll
+            for(int u = 0; u < kUnroll; ++u)
+                acc[u] = neutralA;
+
+            uint64_t const nPacks = n / W;
+            uint64_t const packsPerRow = rowLen / W;
+            auto addr = [&](T const* base, uint64_t p) -> T const*
+            {
+                if constexpr(PITCHED)
+                {
+                    uint64_t const r = p / packsPerRow;
+                    uint64_t const c = p - r * packsPerRow;
+                    return reinterpret_cast<T const*>(reinterpret_cast<char const*>(base) + r * rowPitch) + c * W;
+                }
+                else
+                    return base + p * W;
+            };
+
+            uint64_t const S = static_cast<uint64_t>(gridDim.x) * kBlock;
+            uint64_t i = static_cast<uint64_t>(blockIdx.x) * kBlock + threadIdx.x;
+            for(; i + (kUnroll - 1) * S < nPacks; i += kUnroll * S)
+            {
+                Pack<T, W> x[kUnroll], y[kUnroll];
+#pragma unroll
+                for(int u = 0; u < kUnroll; ++u)
+                {
+                    x[u] = loadPack<T, W>(addr(in0, i + u * S), 0);
+                    if constexpr(XOp == A3B_XFORM_PRODUCT)
+                        y[u] = loadPack<T, W>(addr(in1, i + u * S), 0);
+                    else
+                        y[u] = x[u];
+                }
+#pragma unroll
+                for(int u = 0; u < kUnroll; ++u)
+                    acc[u] = foldPack<T, W, ROp, XOp>(acc[u], x[u], y[u]);
+            }
+#pragma unroll
+            for(int u = 0; u < kUnroll; ++u)
+            {
+                uint64_t const p = i + u * S;
+                if(p < nPacks)
+                {
+                    Pack<T, W> x = loadPack<T, W>(addr(in0, p), 0);
+                    Pack<T, W> y = x;
+                    if constexpr(XOp == A3B_XFORM_PRODUCT)
+                        y = loadPack<T, W>(addr(in1, p), 0);
+                    acc[u] = foldPack<T, W, ROp, XOp>(acc[u], x, y);
+                }
+            }
+            if constexpr(W > 1 && !PITCHED)
+            {
+                uint64_t const e = nPacks * W + static_cast<uint64_t>(blockIdx.x) * kBlock + threadIdx.x;
+                if(e < n)
+                {
+                    T const x = in0[e];
+                    T y = x;
+                    if constexpr(XOp == A3B_XFORM_PRODUCT)
+                        y = in1[e];
+                    acc[0] = combine<A, ROp>(acc[0], widen<A>(xform<XOp>(x, y)));
+                }
+            }
+
+            A v = acc[0];
+#pragma unroll
+            for(int u = 1; u < kUnroll; ++u)
+                v = combine<A, ROp>(v, acc[u]);
+            v = blockReduce<A, ROp>(v, smem);
+
+            if(threadIdx.x == 0)
+            {
+                partials[blockIdx.x] = v;
+                __threadfence();
+                unsigned const t = atomicAdd(&scratch->ticket, 1u);
+                amLast = (t == gridDim.x - 1u);
+            }
+            __syncthreads();
+            if(!amLast)
+                return;
+            __threadfence();
+            // last block: combine all partials in block order (fixed tree => deterministic)
+            A r = neutralA;
+            for(unsigned b = threadIdx.x; b < gridDim.x; b += kBlock)
+                r = combine<A, ROp>(r, __ldcg(partials + b));
+            r = blockReduce<A, ROp>(r, smem);
+            if(threadIdx.x == 0)
+            {
+                writeResult<T, A>(out, r, rawPartial);
+                scratch->ticket = 0u; // ready for the next call on this stream
+            }
+        }
+
+        template<typename T, int W, int ROp, int XOp, bool PITCHED>
+        int launchReduce(
+            cudaStream_t s,
+            T const* in0,
+            T const* in1,
+            uint64_t n,
+            uint64_t rowLen,
+            uint64_t rowPitch,
+            T neutral,
+            void* out,
+            bool raw)
+        {
+            using A = typename AccOf<T, ROp>::type;
+            DeviceProps const* props = nullptr;
+            int rc = currentDevice(&props);
+            if(rc)
+                return rc;
+            static int resident[64] = {0};
+            int& r = resident[props->ordinal];
+            if(r == 0)
+            {
+                int b = 0;
+                A3B_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b, reduceKernel<T, W, ROp, XOp, PITCHED>, kBlock, 0));
+                r = b > 0 ? b : 1;
+            }
+            uint64_t const packs = n / W + 1;
+            uint64_t const want = (packs + static_cast<uint64_t>(kBlock) * kUnroll - 1) / (kBlock * kUnroll);
+            uint64_t const full = static_cast<uint64_t>(props->smCount) * r;
+            int const grid = static_cast<int>(want < full ? (want > 0 ? want : 1) : full);
+
+            void* scr = nullptr;
+            rc = streamScratch(s, kScratchReduce, sizeof(ReduceScratch) + sizeof(A) * static_cast<size_t>(full), &scr);
+            if(rc)
+                return rc;
+            auto* hdr = static_cast<ReduceScratch*>(scr);
+            auto* partials = reinterpret_cast<A*>(hdr + 1);
+            reduceKernel<T, W, ROp, XOp, PITCHED>
+                <<<grid, kBlock, 0, s>>>(in0, in1, n, rowLen, rowPitch, neutral, out, raw, hdr, partials);
+            A3B_CHECK_LAUNCH("transform_reduce launch");
+            return A3B_OK;
+        }
+
+        template<typename T, int ROp, int XOp>
+        int dispatchLayout(
+            cudaStream_t s,
+            T const* in0,
+            T const* in1,
+            uint64_t rows,
+            uint64_t rowLen,
+            uint64_t rowPitch,
+            T neutral,
+            void* out,
+            bool raw)
+        {
+            constexpr int W = 16 / sizeof(T);
+            bool const dense = rows <= 1 || rowPitch == rowLen * sizeof(T);
+            bool const al = aligned16(in0) && (XOp != A3B_XFORM_PRODUCT || aligned16(in1));
+            uint64_t const n = rows * rowLen;
+            if(dense)
+            {
+                if(al)
+                    return launchReduce<T, W, ROp, XOp, false>(s, in0, in1, n, n, 0, neutral, out, raw);
+                return launchReduce<T, 1, ROp, XOp, false>(s, in0, in1, n, n, 0, neutral, out, raw);
+            }
+            if constexpr(XOp != A3B_XFORM_PRODUCT)
+            {
+                if(al && rowLen % W == 0 && rowPitch % 16 == 0)
+                    return launchReduce<T, W, ROp, XOp, true>(s, in0, in1, n, rowLen, rowPitch, neutral, out, raw);
+                return launchReduce<T, 1, ROp, XOp, true>(s, in0, in1, n, rowLen, rowPitch, neutral, out, raw);
+            }
+            setError("pitched layout is supported for single-input reductions only");
+            return A3B_ERR_INVALID;
+        }
+
+        template<typename T, int ROp>
+        int dispatchXform(
+            cudaStream_t s,
+            int xop,
+            T const* in0,
+            T const* in1,
+            uint64_t rows,
+            uint64_t rowLen,
+            uint64_t pitch,
+            T neutral,
+            void* out,
+            bool raw)
+        {
+            switch(xop)
+            {
+            case A3B_XFORM_IDENTITY:
+                return dispatchLayout<T, ROp, A3B_XFORM_IDENTITY>(s, in0, in1, rows, rowLen, pitch, neutral, out, raw);
+            case A3B_XFORM_SQUARE:
+                return dispatchLayout<T, ROp, A3B_XFORM_SQUARE>(s, in0, in1, rows, rowLen, pitch, neutral, out, raw);
+            case A3B_XFORM_PRODUCT:
+                A3B_REQUIRE(in1, "product transform needs two inputs");
+                return dispatchLayout<T, ROp, A3B_XFORM_PRODUCT>(s, in0, in1, rows, rowLen, pitch, neutral, out, raw);
+            default:
+                setError("unknown transform op %d", xop);
+                return A3B_ERR_INVALID;
+            }
+        }
+
+        template<typename T>
+        int dispatchReduce(
+            cudaStream_t s,
+            int rop,
+            int xop,
+            void const* in0,
+            void const* in1,
+            uint64_t rows,
+            uint64_t rowLen,
+            uint64_t pitch,
+            void const* neutral,
+            void* out,
+            bool raw)
+        {
+            T const nv = *static_cast<T const*>(neutral);
+            auto i0 = static_cast<T const*>(in0);
+            auto i1 = static_cast<T const*>(in1);
+            switch(rop)
+            {
+            case A3B_REDUCE_PLUS:
+                return dispatchXform<T, A3B_REDUCE_PLUS>(s, xop, i0, i1, rows, rowLen, pitch, nv, out, raw);
+            case A3B_REDUCE_MIN:
+                return dispatchXform<T, A3B_REDUCE_MIN>(s, xop, i0, i1, rows, rowLen, pitch, nv, out, raw);
+            case A3B_REDUCE_MAX:
+                return dispatchXform<T, A3B_REDUCE_MAX>(s, xop, i0, i1, rows, rowLen, pitch, nv, out, raw);
+            default:
+                setError("unknown reduce op %d", rop);
+                return A3B_ERR_INVALID;
+            }
+        }
+
+        int reduceEntry(
+            a3b_stream_t stream,
+            int dtype,
+            int rop,
+            int xop,
+            void const* in0,
+            void const* in1,
+            uint64_t rows,
+            uint64_t rowLen,
+            uint64_t pitch,
+            void const* neutral,
+            void* out,
+            bool raw)
+        {
+            A3B_REQUIRE(out && neutral, "null out/neutral");
+            A3B_REQUIRE(in0 || rows * rowLen == 0, "null input");
+            auto s = static_cast<cudaStream_t>(stream);
+            switch(dtype)
+            {
+            case A3B_I32:
+                return dispatchReduce<int32_t>(s, rop, xop, in0, in1, rows, rowLen, pitch, neutral, out, raw);
+            case A3B_U32:
+                return dispatchReduce<uint32_t>(s, rop, xop, in0, in1, rows, rowLen, pitch, neutral, out, raw);
+            case A3B_I64:
+                return dispatchReduce<int64_t>(s, rop, xop, in0, in1, rows, rowLen, pitch, neutral, out, raw);
+            case A3B_U64:
+                return dispatchReduce<uint64_t>(s, rop, xop, in0, in1, rows, rowLen, pitch, neutral, out, raw);
+            case A3B_F32:
+                return dispatchReduce<float>(s, rop, xop, in0, in1, rows, rowLen, pitch, neutral, out, raw);
+            case A3B_F64:
+                return dispatchReduce<double>(s, rop, xop, in0, in1, rows, rowLen, pitch, neutral, out, raw);
+            default:
+                setError("unknown dtype %d", dtype);
+                return A3B_ERR_INVALID;
+            }
+        }
+    } // namespace
+} // namespace a3b
+
+using namespace a3b;
+
+extern "C"
+{
+    int a3b_transform_reduce(a3b_stream_t stream, int dtype, int reduce_op, int transform_op, void const* in0,
+                             void const* in1, uint64_t n, void const* neutral, void* out)
+    {
+        return reduceEntry(stream, dtype, reduce_op, transform_op, in0, in1, 1, n, 0, neutral, out, false);
+    }
+
+    int a3b_transform_reduce_partial(a3b_stream_t stream, int dtype, int reduce_op, int transform_op,
+                                     void const* in0, void const* in1, uint64_t n, void const* neutral,
+                                     void* partial_out)
+    {
+        return reduceEntry(stream, dtype, reduce_op, transform_op, in0, in1, 1, n, 0, neutral, partial_out, true);
+    }
+
+    int a3b_reduce_2d(a3b_stream_t stream, int dtype, int reduce_op, void const* in, uint64_t rows, uint64_t row_len,
+                      uint64_t row_pitch_bytes, void const* neutral, void* out)
+    {
+        int const es = dtypeSize(dtype);
+        A3B_REQUIRE(es > 0, "unknown dtype");
+        A3B_REQUIRE(rows <= 1 || row_pitch_bytes >= row_len * static_cast<uint64_t>(es), "row pitch smaller than a row");
+        return reduceEntry(stream, dtype, reduce_op, A3B_XFORM_IDENTITY, in, nullptr, rows, row_len, row_pitch_bytes,
+                           neutral, out, false);
+    }
+}

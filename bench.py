@@ -1,0 +1,390 @@
+"""Benchmark of the primitive path on B200: transformReduce (sum of squares over 2^30 fp32), sharded over ranks.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+    torchrun --nproc-per-node N bench.py --gpus N ...      (one rank per GPU, NCCL)
+
+A step is one pass of the hot path over the workload: every rank reduces its contiguous shard of the 2^30 seeded
+fp32 values (one kernel launch through the C ABI), and for N > 1 the 8-byte partials are combined by an NCCL
+all-reduce. `value` is the whole-job throughput (4 * 2^30 bytes per step / max-over-ranks step time) with the inputs
+resident in HBM; `e2e` is the same step through the C ABI from pinned HOST memory (host->device copy of each rank's
+shard and device->host read of the result inside the timed region). At N = 1 the line also carries `parts`: the other
+kernels the metric names (BabelStream triad and dot at 2^25 fp64, exclusive scan of 2^30 int32, inclusive scan of
+2^28 uint64), each device-timed the same way. The inputs (>= 268 MB per array) exceed the 126 MB L2 in every case.
+
+`--impl reference` times alpaka3's own OpenMP host backend (oracle/_ref, compiled from the reference headers) on the
+host cores for the same metric and workload; under torchrun only rank 0 runs it.
+"""
+import argparse
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "triad/dot/reduce/scan HBM GB/s (fraction of ~8 TB/s) at 1/2/4/8 B200"
+N_SUMSQ = 1 << 30
+SEED = 0x5EED0001
+WORKLOAD = ("transformReduce sum of squares (std::plus, x*x) over 2^30 fp32 uniform[-1,1) from a seeded Philox "
+            "stream, contiguous shards per rank, NCCL all-reduce of the fp64 partials")
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured"
+    except (OSError, KeyError, ValueError):
+        return 6650.0, "fallback"
+
+
+class ClockSampler:
+    """Samples SM clock and clock-event reasons of one GPU through NVML while the timed region runs."""
+
+    REASONS = {
+        "gpu_idle": 0x1, "applications_clocks_setting": 0x2, "sw_power_cap": 0x4, "hw_slowdown": 0x8,
+        "sync_boost": 0x10, "sw_thermal_slowdown": 0x20, "hw_thermal_slowdown": 0x40, "hw_power_brake_slowdown": 0x80,
+    }
+
+    def __init__(self, pci_bus_id, period_s=0.002):
+        self.period = period_s
+        self.samples, self.reasons, self.max_mhz = [], set(), None
+        self._stop = threading.Event()
+        self._t = None
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self.nv = pynvml
+            self.h = pynvml.nvmlDeviceGetHandleByPciBusId(pci_bus_id)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+        except Exception:  # noqa: BLE001 - clocks are reported as unavailable
+            self.nv = None
+
+    def _run(self):
+        while not self._stop.is_set():
+            self._sample()
+            time.sleep(self.period)
+
+    def _sample(self):
+        try:
+            self.samples.append(self.nv.nvmlDeviceGetClockInfo(self.h, self.nv.NVML_CLOCK_SM))
+            r = self.nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+            for name, bit in self.REASONS.items():
+                if r & bit:
+                    self.reasons.add(name)
+        except Exception:  # noqa: BLE001
+            pass
+
+    def start(self):
+        if self.nv:
+            self._t = threading.Thread(target=self._run, daemon=True)
+            self._t.start()
+
+    def stop(self):
+        if self.nv and self._t:
+            self._stop.set()
+            self._t.join()
+            self._sample()
+
+    def summary(self):
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": ["unavailable"], "samples": 0}
+        return {"sm_mhz": statistics.median(self.samples), "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(self.reasons - {"gpu_idle"}), "samples": len(self.samples)}
+
+
+def pci_bus_id(torch, ordinal):
+    p = torch.cuda.get_device_properties(ordinal)
+    return "%08X:%02X:%02X.0" % (getattr(p, "pci_domain_id", 0), p.pci_bus_id, p.pci_device_id)
+
+
+# ------------------------------------------------------------------------------------------------ device timing
+def time_steps(torch, dist_on, step, steps, warmup, kernel_events=None):
+    """W untimed steps, then K steps between barrier+sync on both sides; returns (ms per step, kernel ms avg)."""
+    for _ in range(warmup):
+        step(None)
+    torch.cuda.synchronize()
+    if dist_on:
+        import torch.distributed as dist
+        dist.barrier()
+    torch.cuda.synchronize()
+    s = torch.cuda.current_stream()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record(s)
+    for k in range(steps):
+        step(ev[k])
+    t1.record(s)
+    torch.cuda.synchronize()
+    if dist_on:
+        import torch.distributed as dist
+        dist.barrier()
+    total = t0.elapsed_time(t1)
+    kern = statistics.mean(a.elapsed_time(b) for a, b in ev)
+    return total / steps, kern
+
+
+def max_over_ranks(torch, dist_on, v):
+    if not dist_on:
+        return v
+    import torch.distributed as dist
+    t = torch.tensor([v], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return t.item()
+
+
+def run_b200(args):
+    import torch
+    from alpaka3_b200 import algo, capi, dist as adist
+
+    world, rank, local = adist.init()
+    dist_on = world > 1
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    capi.lib()
+    peak, peak_kind = peaks()
+
+    # ---------------------------------------------------------------- headline: sum of squares, 2^30 fp32
+    b, e = adist.shard_range(N_SUMSQ, rank, world)
+    n_local = e - b
+    x = torch.empty(n_local, dtype=torch.float32, device=dev)
+    algo.random_f32(x, SEED, -1.0, 1.0, start=b)
+    out = torch.empty(1, dtype=torch.float32, device=dev)
+    partial = torch.empty(1, dtype=torch.float64, device=dev)
+    s = torch.cuda.current_stream()
+    launches = [0]
+
+    def step(ev):
+        if ev:
+            ev[0].record(s)
+        if dist_on:
+            algo.transform_reduce_partial("plus", "square", x, partial=partial)
+        else:
+            algo.transform_reduce(0.0, out, "plus", "square", x)
+        if ev:
+            ev[1].record(s)
+            launches[0] += 1
+        if dist_on:
+            adist.allreduce_partial(partial, "plus")
+
+    sampler = ClockSampler(pci_bus_id(torch, local))
+    sampler.start()
+    ms, kern_ms = time_steps(torch, dist_on, step, args.steps, args.warmup)
+    sampler.stop()
+    ms = max_over_ranks(torch, dist_on, ms)
+    total_bytes = 4.0 * N_SUMSQ
+    value = total_bytes / (ms * 1e-3) / 1e9
+    kern_gbs = 4.0 * n_local / (kern_ms * 1e-3) / 1e9
+    result = float(partial.item()) if dist_on else float(out.item())
+
+    # ---------------------------------------------------------------- e2e: host buffers through the C ABI
+    e2e = None
+    if not args.no_e2e:
+        host = torch.empty(n_local, dtype=torch.float32, pin_memory=True)
+        host.copy_(x.cpu())
+        res_host = torch.empty(1, dtype=torch.float64 if dist_on else torch.float32, pin_memory=True)
+        sh = algo.stream_handle()
+        import ctypes
+
+        def e2e_step(ev):
+            capi.call("a3b_memcpy_async", ctypes.c_void_p(x.data_ptr()), ctypes.c_void_p(host.data_ptr()),
+                      4 * n_local, sh)
+            if dist_on:
+                algo.transform_reduce_partial("plus", "square", x, partial=partial)
+                adist.allreduce_partial(partial, "plus")
+                src = partial
+            else:
+                algo.transform_reduce(0.0, out, "plus", "square", x)
+                src = out
+            capi.call("a3b_memcpy_async", ctypes.c_void_p(res_host.data_ptr()), ctypes.c_void_p(src.data_ptr()),
+                      src.element_size(), sh)
+
+        e_steps = max(1, min(args.steps, 10))
+        e_ms, _ = time_steps(torch, dist_on, e2e_step, e_steps, 1)
+        e_ms = max_over_ranks(torch, dist_on, e_ms)
+        e2e = {"value": total_bytes / (e_ms * 1e-3) / 1e9, "unit": "GB/s", "h2d_bytes_per_step": 4 * N_SUMSQ,
+               "d2h_bytes_per_step": (8 if dist_on else 4) * world, "steps": e_steps,
+               "path": "a3b_memcpy_async(H2D, pinned) + a3b_transform_reduce + a3b_memcpy_async(D2H)"}
+        del host
+
+    # ---------------------------------------------------------------- other kernels of the metric (N = 1)
+    parts = None
+    if world == 1 and not args.no_parts:
+        parts = bench_parts(torch, algo, dev, args, peak)
+
+    # ---------------------------------------------------------------- CPU baseline: alpaka3's OpenMP backend
+    cpu = None
+    if world == 1 and rank == 0 and not args.no_cpu:
+        cpu = cpu_baseline(budget_s=args.cpu_seconds)
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms, 5), "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded Philox4x32-10, uniform [-1,1))",
+            "config": {"workload": WORKLOAD, "n": N_SUMSQ, "bytes_per_step": int(total_bytes),
+                       "per_rank_elements": n_local, "l2": "inputs larger than L2 (4.29 GB total, >= 537 MB per GPU)",
+                       "parallelism": f"shard{world}+allreduce" if dist_on else "single GPU"},
+            "result": result,
+            "roofline": {"bound": "hbm", "achieved": round(kern_gbs, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(kern_gbs / peak, 4), "peak_kind": peak_kind,
+                         "traffic": SUMSQ_TRAFFIC_PER_LAUNCH(n_local),
+                         "kernel": "reduceKernel<float,4,plus,square> (a3b_transform_reduce)",
+                         "kernel_ms": round(kern_ms, 5)},
+            "e2e": e2e, "gpu_launches": launches[0], "clocks": sampler.summary(),
+        }
+        if cpu:
+            line["cpu_baseline"] = cpu
+        if parts:
+            line["parts"] = parts
+        print(json.dumps(line), flush=True)
+    if dist_on:
+        import torch.distributed as dist
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def SUMSQ_TRAFFIC_PER_LAUNCH(n_local):
+    """DRAM bytes per launch from the committed ncu capture (profiles/), scaled by elements; None if not captured."""
+    p = os.path.join(ROOT, "profiles", "traffic.json")
+    try:
+        with open(p) as f:
+            t = json.load(f)["sumsq_f32_bytes_per_element"]
+        return int(t * n_local)
+    except (OSError, KeyError, ValueError):
+        return None
+
+
+def bench_parts(torch, algo, dev, args, peak):
+    parts = {}
+    steps = max(args.steps, 20)
+
+    def measure(name, step, bytes_per_step, extra=None):
+        ms, kern = time_steps(torch, False, lambda ev: _wrap(torch, ev, step), steps, max(args.warmup, 3))
+        gbs = bytes_per_step / (kern * 1e-3) / 1e9
+        d = {"GB/s": round(gbs, 1), "frac": round(gbs / peak, 4), "kernel_ms": round(kern, 5),
+             "bytes_per_step": int(bytes_per_step)}
+        if extra:
+            d.update(extra)
+        parts[name] = d
+
+    n = 1 << 25
+    a, b, c = (torch.empty(n, dtype=torch.float64, device=dev) for _ in range(3))
+    algo.babelstream("init", a, b, c)
+    measure("triad_f64_2^25", lambda: algo.babelstream("triad", a, b, c), 3 * 8 * n)
+    measure("copy_f64_2^25", lambda: algo.babelstream("copy", a, b, c), 2 * 8 * n)
+    out = torch.empty(1, dtype=torch.float64, device=dev)
+    measure("dot_f64_2^25", lambda: algo.transform_reduce(0.0, out, "plus", "product", a, b), 2 * 8 * n)
+    del a, b, c
+    n = 1 << 30
+    xi = torch.empty(n, dtype=torch.int32, device=dev)
+    algo.random_u32(xi, SEED, shift=28)
+    yi = torch.empty_like(xi)
+    measure("exclusive_scan_i32_2^30", lambda: algo.exclusive_scan(yi, xi), 2 * 4 * n)
+    del xi, yi
+    n = 1 << 28
+    xu = torch.empty(n, dtype=torch.int64, device=dev)
+    algo.random_u64(xu, SEED)
+    yu = torch.empty_like(xu)
+    measure("inclusive_scan_u64_2^28", lambda: algo.inclusive_scan(yu, xu), 2 * 8 * n)
+    del xu, yu
+    torch.cuda.synchronize()
+    return parts
+
+
+def _wrap(torch, ev, fn):
+    s = torch.cuda.current_stream()
+    if ev:
+        ev[0].record(s)
+    fn()
+    if ev:
+        ev[1].record(s)
+
+
+def cpu_baseline(budget_s=8.0, n=1 << 28):
+    """alpaka3's own transformReduce on exec::cpuOmpBlocks over a 2^28 fp32 sample (1.07 GB), repeated for about
+    budget_s seconds; GB/s of input read."""
+    try:
+        from oracle.oracle import Port, Ref
+        ref, port = Ref(), Port()
+    except Exception as e:  # noqa: BLE001
+        return {"value": None, "unit": "GB/s", "kind": "reference", "unavailable": str(e)}
+    x = port.gen_f32(n, -1.0, 1.0, seed=SEED)
+    ref.sumsq(x)  # warm-up
+    times = []
+    t_end = time.perf_counter() + budget_s
+    while time.perf_counter() < t_end or len(times) < 3:
+        t0 = time.perf_counter()
+        ref.sumsq(x)
+        times.append(time.perf_counter() - t0)
+    best = min(times)
+    return {"value": round(4.0 * n / best / 1e9, 2), "unit": "GB/s", "cores": ref.num_threads(), "kind": "reference",
+            "sample": f"alpaka3 onHost::transformReduce(exec::cpuOmpBlocks) over 2^28 fp32 (first 2^28 elements of the "
+                      f"workload's stream), best of {len(times)} runs in {budget_s:.0f} s",
+            "median_GB/s": round(4.0 * n / statistics.median(times) / 1e9, 2)}
+
+
+def run_reference(args):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    try:
+        from oracle.oracle import Port, Ref
+        ref, port = Ref(), Port()
+    except Exception as e:  # noqa: BLE001
+        print(json.dumps({"impl": "reference", "unavailable": f"alpaka3 host backend not built: {e}"}), flush=True)
+        return
+    x = port.gen_f32(N_SUMSQ, -1.0, 1.0, seed=SEED)
+    for _ in range(args.warmup):
+        ref.sumsq(x)
+    times = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        r = ref.sumsq(x)
+        times.append(time.perf_counter() - t0)
+    ms = 1e3 * sum(times) / len(times)
+    value = 4.0 * N_SUMSQ / (ms * 1e-3) / 1e9
+    cores = ref.num_threads()
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 3), "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded Philox4x32-10, uniform [-1,1))",
+        "config": {"workload": WORKLOAD.replace(", contiguous shards per rank, NCCL all-reduce of the fp64 partials",
+                                                "") + ", whole input on the host", "n": N_SUMSQ,
+                   "bytes_per_step": 4 * N_SUMSQ, "parallelism": "host OpenMP"},
+        "result": float(r),
+        "cpu_baseline": {"value": round(value, 2), "unit": "GB/s", "cores": cores, "kind": "reference",
+                         "sample": "alpaka3 onHost::transformReduce(exec::cpuOmpBlocks) over the full 2^30 fp32 "
+                                   "workload per step"},
+        "e2e": {"value": round(value, 2), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--no-parts", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=8.0)
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_b200(args)
+
+
+if __name__ == "__main__":
+    main()

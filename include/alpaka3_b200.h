@@ -1,0 +1,229 @@
+/* alpaka3_b200 -- C ABI of the B200 (sm_100a) data-parallel primitive library.
+ *
+ * Plain pointers and sizes only: every device pointer is a CUDA device (or managed) address on the device that is
+ * current on the calling thread, every stream is a cudaStream_t passed as void*, and every entry point returns an
+ * int status (A3B_OK == 0). On failure a3b_last_error() returns a message for the calling thread. All entry points
+ * are asynchronous with respect to the host unless stated otherwise; results are visible after the stream is
+ * synchronised.
+ *
+ * Each entry point names the alpaka3 interface whose backend dispatch it replaces (paths inside the alpaka3 project).
+ */
+#ifndef ALPAKA3_B200_H
+#define ALPAKA3_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define A3B_VERSION 100
+
+#if defined(__GNUC__)
+#define A3B_API __attribute__((visibility("default")))
+#else
+#define A3B_API
+#endif
+
+typedef void* a3b_stream_t; /* cudaStream_t */
+
+enum a3b_status
+{
+    A3B_OK = 0,
+    A3B_ERR_INVALID = 1,     /* bad argument (null pointer, unsupported dtype/op combination, bad size) */
+    A3B_ERR_CUDA = 2,        /* a CUDA runtime call failed; message has the CUDA error string */
+    A3B_ERR_UNSUPPORTED = 3, /* no device / wrong architecture */
+    A3B_ERR_TIMEOUT = 4,     /* a bounded device-side wait gave up (reported by a3b_get_device_error) */
+    A3B_ERR_NOMEM = 5,
+    A3B_ERR_TOO_LARGE = 6
+};
+
+enum a3b_dtype
+{
+    A3B_I32 = 0,
+    A3B_U32 = 1,
+    A3B_I64 = 2,
+    A3B_U64 = 3,
+    A3B_F32 = 4,
+    A3B_F64 = 5
+};
+
+/* binary reduce functors: std::plus, ScalarFunc{min}, ScalarFunc{max} (test/unit/algorithm/reduce.cpp:22-56) */
+enum a3b_reduce_op
+{
+    A3B_REDUCE_PLUS = 0,
+    A3B_REDUCE_MIN = 1,
+    A3B_REDUCE_MAX = 2
+};
+
+/* transform functors recognised on the C path: identity (onHost::reduce), x*x, a*b (BabelStream DotMultiplication) */
+enum a3b_transform_op
+{
+    A3B_XFORM_IDENTITY = 0,
+    A3B_XFORM_SQUARE = 1,
+    A3B_XFORM_PRODUCT = 2
+};
+
+/* BabelStream element-wise kernels (benchmark/babelstream/src/babelStreamMainTest.cpp:78-133) */
+enum a3b_stream_kind
+{
+    A3B_STREAM_INIT = 0,   /* a = init[0], b = init[1], c = init[2] */
+    A3B_STREAM_COPY = 1,   /* c = a */
+    A3B_STREAM_MUL = 2,    /* b = scalar * c */
+    A3B_STREAM_ADD = 3,    /* c = a + b */
+    A3B_STREAM_TRIAD = 4,  /* a = b + scalar * c */
+    A3B_STREAM_NSTREAM = 5 /* a = a + b + scalar * c */
+};
+
+/* element-wise transforms for onHost::transform / onHost::concurrent with recognised functors */
+enum a3b_map_kind
+{
+    A3B_MAP_COPY = 0,  /* out = in0 */
+    A3B_MAP_SCALE = 1, /* out = alpha * in0 */
+    A3B_MAP_ADD = 2,   /* out = in0 + in1 */
+    A3B_MAP_MUL = 3,   /* out = in0 * in1 */
+    A3B_MAP_AXPY = 4,  /* out = in0 + alpha * in1 (each operation rounded on its own) */
+    A3B_MAP_SQUARE = 5 /* out = in0 * in0 */
+};
+
+typedef struct a3b_device_info
+{
+    int ordinal;
+    int sm_count;
+    int cc_major;
+    int cc_minor;
+    uint64_t global_mem_bytes;
+    uint64_t l2_bytes;
+    int max_threads_per_block;
+    int warp_size;
+    char name[128];
+} a3b_device_info;
+
+/* ------------------------------------------------------------------------------------------------- runtime */
+
+A3B_API int a3b_version(void);
+A3B_API const char* a3b_last_error(void);
+/* onHost::DeviceSelector::getDeviceCount / getDeviceProperties (include/alpaka/onHost/DeviceProperties.hpp:28-56) */
+A3B_API int a3b_device_count(int* count);
+A3B_API int a3b_device_info_get(int ordinal, a3b_device_info* info);
+/* onHost::alloc / allocDeferred: stream-ordered device allocation (include/alpaka/onHost/Queue.hpp:410) */
+A3B_API int a3b_malloc_async(void** ptr, size_t bytes, a3b_stream_t stream);
+A3B_API int a3b_free_async(void* ptr, a3b_stream_t stream);
+/* onHost::memcpy (include/alpaka/onHost/Queue.hpp:237): any direction, one cudaMemcpyAsync */
+A3B_API int a3b_memcpy_async(void* dst, void const* src, size_t bytes, a3b_stream_t stream);
+/* onHost::wait(queue) (include/alpaka/onHost/interface.hpp:142) */
+A3B_API int a3b_stream_synchronize(a3b_stream_t stream);
+/* Reads (and with clear != 0 resets) the device-side error word of the current device: bit 0 = a bounded wait timed
+ * out (A3B_ERR_TIMEOUT). Synchronises `stream`. */
+A3B_API int a3b_get_device_error(a3b_stream_t stream, uint32_t* error_bits, int clear);
+/* Limit in nanoseconds for every device-side spin-wait issued afterwards by this process (default 1 s). */
+A3B_API int a3b_set_wait_timeout_ns(uint64_t ns);
+
+/* ------------------------------------------------------------------------------- element-wise (transform) */
+
+/* BabelStream kernels: queue.enqueue(FrameSpec, KernelBundle{SimdForEachKernel{}, Simd<Op>{}, a, b, c})
+ * (benchmark/babelstream/src/babelStreamMainTest.cpp:285-364). dtype A3B_F32 or A3B_F64. init may be null unless
+ * kind == A3B_STREAM_INIT. Every floating-point operation is rounded on its own (no contraction). */
+A3B_API int a3b_babelstream(a3b_stream_t stream, int kind, int dtype, void* a, void* b, void* c, uint64_t n, double scalar,
+                    double const* init);
+
+/* onHost::transform(queue, out, fn, in0[, in1]) with a recognised fn (include/alpaka/onHost/algo/transform.hpp:50-88).
+ * in1 is ignored for unary kinds. Integer dtypes wrap; alpha is converted to dtype first. */
+A3B_API int a3b_transform(a3b_stream_t stream, int kind, int dtype, void* out, void const* in0, void const* in1, uint64_t n,
+                  double alpha);
+
+/* onHost::fill (include/alpaka/onHost/Queue.hpp:346): value points to one host element of dtype */
+A3B_API int a3b_fill(a3b_stream_t stream, int dtype, void* out, uint64_t n, void const* value);
+
+/* onHost::iota (include/alpaka/onHost/algo/iota.hpp:29-85): out[i] = start + i (host start value of dtype) */
+A3B_API int a3b_iota(a3b_stream_t stream, int dtype, void* out, uint64_t n, void const* start);
+
+/* nBody drift, onHost::concurrent(..., UpdatePositions{dt}, x, y, z, vx, vy, vz) (example/nBody/src/Kernels.hpp:126-142):
+ * x = x + vx*dt per component, fp32 */
+A3B_API int a3b_nbody_update_positions(a3b_stream_t stream, float* x, float* y, float* z, float const* vx, float const* vy,
+                               float const* vz, uint64_t n, float dt);
+
+/* Seeded Philox4x32-10 streams (counter = start + element index, key = seed), identical to the CPU oracle:
+ *   u32: word0 >> shift;   u64: (word1 << 32) | word0;   f32: lo + (hi - lo) * ((word0 >> 8) * 2^-24). */
+A3B_API int a3b_random_u32(a3b_stream_t stream, uint32_t* out, uint64_t n, uint64_t seed, uint64_t start, int shift);
+A3B_API int a3b_random_u64(a3b_stream_t stream, uint64_t* out, uint64_t n, uint64_t seed, uint64_t start);
+A3B_API int a3b_random_f32(a3b_stream_t stream, float* out, uint64_t n, uint64_t seed, uint64_t start, float lo, float hi);
+
+/* ---------------------------------------------------------------------------------------------- reductions */
+
+/* onHost::transformReduce(queue, neutral, out, reduceFn, transformFn, in0[, in1])
+ * (include/alpaka/onHost/algo/transformReduce.hpp:59-90; kernel internal/transformReduce.hpp:23-202).
+ * out: device pointer to ONE element of dtype, written with the final value (no pre-fill launch needed).
+ * neutral: host pointer to one element of dtype. One launch; the final combination runs in the last block in a fixed
+ * order, so a given (device, n) always gives the same bits. fp32 inputs are accumulated in fp64 inside the kernel;
+ * integer + wraps (two's complement). */
+A3B_API int a3b_transform_reduce(a3b_stream_t stream, int dtype, int reduce_op, int transform_op, void const* in0,
+                         void const* in1, uint64_t n, void const* neutral, void* out);
+
+/* Same, but the per-block partials are left as fp64 (float dtypes) / 64-bit integers in partial_out[0] instead of
+ * being rounded to dtype: used to combine shards across GPUs before the final rounding. */
+A3B_API int a3b_transform_reduce_partial(a3b_stream_t stream, int dtype, int reduce_op, int transform_op, void const* in0,
+                                 void const* in1, uint64_t n, void const* neutral, void* partial_out);
+
+/* onHost::reduce(queue, neutral, out, reduceFn, in) (include/alpaka/onHost/algo/reduce.hpp:28-79) over a pitched
+ * 2-D view: `rows` rows of `row_len` elements, consecutive rows `row_pitch_bytes` apart (rows = 1 for 1-D data).
+ * N-D alpaka buffers whose slower dimensions are dense multiples of the row pitch map onto this form. */
+A3B_API int a3b_reduce_2d(a3b_stream_t stream, int dtype, int reduce_op, void const* in, uint64_t rows, uint64_t row_len,
+                  uint64_t row_pitch_bytes, void const* neutral, void* out);
+
+/* ------------------------------------------------------------------------------------------------------ scan */
+
+/* onHost::getScanBufferSize<T>(extents) (include/alpaka/onHost/algo/scan.hpp:26-30): bytes of the caller buffer that
+ * a3b_scan accepts for n elements of dtype. */
+A3B_API size_t a3b_scan_buffer_size(int dtype, uint64_t n);
+
+/* onHost::inclusiveScan / exclusiveScan / *InPlace (include/alpaka/onHost/algo/scan.hpp:45-218), operator +,
+ * exclusive identity 0. One launch (single-pass decoupled look-back). in == out is allowed (in-place).
+ * buffer: optional caller scratch of at least a3b_scan_buffer_size bytes (any contents; it is cleared on the
+ *         stream); null uses a scratch cached by the library per (device, stream).
+ * carry_in: optional DEVICE pointer to one element added to every output (the sum of all preceding shards when a
+ *         scan is split across GPUs); null means 0. Integer arithmetic wraps (two's complement). */
+A3B_API int a3b_scan(a3b_stream_t stream, int dtype, int inclusive, void const* in, void* out, uint64_t n,
+             void const* carry_in, void* buffer, size_t buffer_bytes);
+
+/* Failure-detection test hook: runs a3b_scan (no caller buffer) with tile `stall_tile` never publishing its status,
+ * so every later tile's bounded look-back gives up after the configured timeout, raises bit 0 of the device error
+ * word and returns. The output is undefined; the context stays usable. */
+A3B_API int a3b_scan_debug_stall(a3b_stream_t stream, int dtype, void const* in, void* out, uint64_t n, uint64_t stall_tile);
+
+/* ----------------------------------------------------------------------------------------------------- nBody */
+
+/* UpdateVelocitiesKernel (example/nBody/src/Kernels.hpp:24-124) for the i-bodies [i_begin, i_begin + i_count) against
+ * all n_all j-bodies: v_i += dt * sum_j m_j d_ij / ((|d_ij|^2 + eps)^3)^(1/2), d_ij = p_j - p_i.
+ * m, x, y, z hold all n_all bodies; vx, vy, vz hold the i_count local velocities. fp32, SoA. */
+A3B_API int a3b_nbody_update_velocities(a3b_stream_t stream, float const* m, float const* x, float const* y, float const* z,
+                                uint64_t n_all, uint64_t i_begin, uint64_t i_count, float* vx, float* vy, float* vz,
+                                float dt, float eps);
+
+/* One full nBody time step for the local bodies (nBody.cpp:188-205): the velocity kick above for [i_begin,
+ * i_begin + i_count), then the drift x += v*dt of those bodies' positions (x + i_begin ...), in one call. The positions
+ * of all n_all bodies are read before any is moved (the drift runs after every force is known). */
+A3B_API int a3b_nbody_step(a3b_stream_t stream, float const* m, float* x, float* y, float* z, uint64_t n_all,
+                   uint64_t i_begin, uint64_t i_count, float* vx, float* vy, float* vz, float dt, float eps);
+
+/* ------------------------------------------------------------------------------------------------------ heat */
+
+/* StencilKernel (example/heatEquation2D/src/StencilKernel.hpp:26-86): one explicit 5-point Jacobi step on a row-major
+ * fp64 grid of (rows + 2) x (cols + 2) cells (1-cell halo ring), consecutive rows `pitch_elems` apart. Updates interior
+ * rows [row_begin, row_end) (1 <= row_begin <= row_end <= rows + 1) and all interior columns:
+ *   next = cur*(1 - 2rX - 2rY) + west*rX + east*rX + north*rY + south*rY   (left to right, each op rounded).
+ * The halo ring of `next` is not written. */
+A3B_API int a3b_heat_step(a3b_stream_t stream, double const* cur, double* next, uint64_t rows, uint64_t cols,
+                  uint64_t pitch_elems, uint64_t row_begin, uint64_t row_end, double rX, double rY);
+
+/* Initial field of the heat workload: interior sin(pi*j*dx)*sin(pi*(i + row_offset)*dy), ring set to 0 only at the
+ * global boundary (row i of this slab is global row i + row_offset). grid as in a3b_heat_step, rows = local rows. */
+A3B_API int a3b_heat_init(a3b_stream_t stream, double* u, uint64_t rows, uint64_t cols, uint64_t pitch_elems,
+                  uint64_t row_offset, uint64_t global_rows, double dx, double dy);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* ALPAKA3_B200_H */

@@ -1,0 +1,47 @@
+"""Build recipe for the CPU oracle (test infrastructure, never the product path).
+
+* ``oracle/liboracle.so``     -- the plain-C restatement in ``oracle.c`` (always built).
+* ``oracle/_ref/libalpaka_ref.so`` -- alpaka3's own host backend behind ``ref_harness.cpp``; built only where the
+  reference tree exists (``build_ref.sh``). The built file travels with the repository snapshot; the source tree it
+  is compiled from does not.
+"""
+import os
+import subprocess
+import sys
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ORACLE_SO = os.path.join(HERE, "liboracle.so")
+REF_SO = os.path.join(HERE, "_ref", "libalpaka_ref.so")
+REFERENCE_ROOT = os.environ.get("ALPAKA_REFERENCE_ROOT", "/root/reference")
+
+
+def _stale(target, sources):
+    if not os.path.exists(target):
+        return True
+    t = os.path.getmtime(target)
+    return any(os.path.getmtime(s) > t for s in sources)
+
+
+def build_oracle(force=False):
+    src = os.path.join(HERE, "oracle.c")
+    if force or _stale(ORACLE_SO, [src, __file__]):
+        cmd = ["gcc", "-std=c11", "-O3", "-march=x86-64-v3", "-fopenmp", "-ffp-contract=off", "-fPIC", "-shared",
+               "-o", ORACLE_SO + ".tmp", src, "-lm"]
+        subprocess.check_call(cmd)
+        os.replace(ORACLE_SO + ".tmp", ORACLE_SO)
+    return ORACLE_SO
+
+
+def build_ref(force=False):
+    if not os.path.isdir(os.path.join(REFERENCE_ROOT, "include", "alpaka")):
+        return REF_SO if os.path.exists(REF_SO) else None
+    srcs = [os.path.join(HERE, "ref_harness.cpp"), os.path.join(HERE, "build_ref.sh")]
+    if force or _stale(REF_SO, srcs):
+        subprocess.check_call(["bash", os.path.join(HERE, "build_ref.sh"), REFERENCE_ROOT])
+    return REF_SO
+
+
+if __name__ == "__main__":
+    force = "--force" in sys.argv
+    print(build_oracle(force))
+    print(build_ref(force))

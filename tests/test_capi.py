@@ -1,0 +1,52 @@
+"""CPU: the C-ABI library loads and exports every entry point the public header declares (no GPU calls)."""
+import ctypes
+import os
+import re
+
+from conftest import ROOT
+
+
+def _declared():
+    names = set()
+    for fn in os.listdir(os.path.join(ROOT, "include")):
+        if fn.endswith(".h"):
+            src = open(os.path.join(ROOT, "include", fn)).read()
+            src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+            names |= set(re.findall(r"\b(a3b_[a-z0-9_]+)\s*\(", src))
+    return names
+
+
+def test_header_declares_entry_points():
+    names = _declared()
+    assert {"a3b_transform_reduce", "a3b_scan", "a3b_babelstream", "a3b_heat_step",
+            "a3b_nbody_update_velocities"} <= names
+
+
+def test_library_exports_every_declared_symbol():
+    from alpaka3_b200 import capi
+    lib = ctypes.CDLL(capi.LIB_PATH)
+    missing = [n for n in sorted(_declared()) if not hasattr(lib, n)]
+    assert not missing, missing
+
+
+def test_binding_covers_header():
+    from alpaka3_b200 import capi
+    assert _declared() == set(capi.SIGNATURES)
+
+
+def test_version_and_scan_buffer_size():
+    from alpaka3_b200 import capi
+    L = capi.lib()
+    assert L.a3b_version() == 100
+    # 4-byte types: 64-byte header + one 8-byte status word per 4096-element tile (256-byte aligned)
+    assert L.a3b_scan_buffer_size(capi.U32, 1 << 30) == 64 + (1 << 18) * 8
+    assert L.a3b_scan_buffer_size(capi.U32, 1) == 64 + 256
+    assert L.a3b_scan_buffer_size(99, 10) == 0
+
+
+def test_invalid_arguments_rejected_without_gpu():
+    from alpaka3_b200 import capi
+    L = capi.lib()
+    rc = L.a3b_babelstream(None, capi.TRIAD, capi.I32, None, None, None, 10, 0.4, None)
+    assert rc == capi.ERR_INVALID
+    assert "null" in capi.last_error()
