@@ -8,7 +8,8 @@ import ctypes
 import os
 
 _HERE = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.path.join(_HERE, "lib", "libalpaka3_b200.so")
+# A3B_LIBRARY selects another build of the same library (e.g. a tuning variant); default: the in-tree build
+LIB_PATH = os.environ.get("A3B_LIBRARY") or os.path.join(_HERE, "lib", "libalpaka3_b200.so")
 
 # status codes
 OK, ERR_INVALID, ERR_CUDA, ERR_UNSUPPORTED, ERR_TIMEOUT, ERR_NOMEM, ERR_TOO_LARGE = range(7)

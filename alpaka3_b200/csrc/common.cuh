@@ -72,7 +72,10 @@ namespace a3b
         kScratchNbody = 2,
         kScratchSlots = 3
     };
-    int streamScratch(cudaStream_t stream, int slot, size_t bytes, void** ptr);
+    // With `epoch` non-null, also hands out the next call epoch of this scratch (30 bits, never 0): kernels that tag
+    // their scratch words with the epoch need no clearing between calls on the stream.
+    int streamScratch(cudaStream_t stream, int slot, size_t bytes, void** ptr, unsigned* epoch = nullptr);
+    constexpr unsigned kScratchEpochMask = 0x3FFFFFFFu;
 
 
     inline int dtypeSize(int dtype)

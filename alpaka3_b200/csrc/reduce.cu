@@ -89,7 +89,7 @@ namespace a3b
         }
 
         template<typename T, int W>
-        struct alignas(16) Pack
+        struct alignas(W * sizeof(T) >= 32 ? 32 : 16) Pack
         {
             T v[W];
         };
@@ -97,7 +97,19 @@ namespace a3b
         template<typename T, int W>
         __device__ __forceinline__ Pack<T, W> loadPack(T const* base, uint64_t packIdx)
         {
-            if constexpr(W * sizeof(T) == 16)
+            if constexpr(W * sizeof(T) == 32)
+            {
+                // 256-bit load (sm_100), evict-first: the data is read once
+                unsigned long long r0, r1, r2, r3;
+                asm volatile("ld.global.cs.v4.u64 {%0, %1, %2, %3}, [%4];"
+                             : "=l"(r0), "=l"(r1), "=l"(r2), "=l"(r3)
+                             : "l"(base + packIdx * W));
+                unsigned long long raw[4] = {r0, r1, r2, r3};
+                Pack<T, W> p;
+                memcpy(&p, raw, 32);
+                return p;
+            }
+            else if constexpr(W * sizeof(T) == 16)
             {
                 uint4 raw = __ldcs(reinterpret_cast<uint4 const*>(base) + packIdx);
                 return *reinterpret_cast<Pack<T, W>*>(&raw);
@@ -367,9 +379,13 @@ namespace a3b
             constexpr int W = 16 / sizeof(T);
             bool const dense = rows <= 1 || rowPitch == rowLen * sizeof(T);
             bool const al = aligned16(in0) && (XOp != A3B_XFORM_PRODUCT || aligned16(in1));
+            auto a32 = [](void const* p) { return (reinterpret_cast<uintptr_t>(p) & 31u) == 0u; };
+            bool const al32 = a32(in0) && (XOp != A3B_XFORM_PRODUCT || a32(in1));
             uint64_t const n = rows * rowLen;
             if(dense)
             {
+                if(al32)
+                    return launchReduce<T, 2 * W, ROp, XOp, false>(s, in0, in1, n, n, 0, neutral, out, raw);
                 if(al)
                     return launchReduce<T, W, ROp, XOp, false>(s, in0, in1, n, n, 0, neutral, out, raw);
                 return launchReduce<T, 1, ROp, XOp, false>(s, in0, in1, n, n, 0, neutral, out, raw);

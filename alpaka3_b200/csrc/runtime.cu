@@ -29,6 +29,7 @@ namespace a3b
         {
             void* ptr = nullptr;
             size_t bytes = 0;
+            unsigned epoch = 0; // last epoch handed out for this scratch (calls on one stream are ordered)
         };
 
         std::mutex gScratchMutex;
@@ -90,7 +91,7 @@ namespace a3b
         return gTimeoutNs.load(std::memory_order_relaxed);
     }
 
-    int streamScratch(cudaStream_t stream, int slot, size_t bytes, void** ptr)
+    int streamScratch(cudaStream_t stream, int slot, size_t bytes, void** ptr, unsigned* epoch)
     {
         int dev = 0;
         A3B_CUDA(cudaGetDevice(&dev));
@@ -115,6 +116,13 @@ namespace a3b
             s.bytes = want;
         }
         *ptr = s.ptr;
+        if(epoch)
+        {
+            s.epoch = (s.epoch + 1u) & kScratchEpochMask;
+            if(s.epoch == 0u)
+                s.epoch = 1u;
+            *epoch = s.epoch;
+        }
         return A3B_OK;
     }
 

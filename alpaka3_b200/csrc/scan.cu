@@ -4,20 +4,23 @@
 // include/alpaka/onHost/algo/internal/scan.hpp:114-472 (about 4N-5N elements of traffic and 2*levels launches) with
 // one launch that reads every element once and writes it once (2N).
 //
-// Tile = 256 threads x 4 rounds x one 16-byte pack per thread (4096 x 4-byte or 2048 x 8-byte elements). Warp w of a
-// tile owns a contiguous segment; in round r lane l holds the pack at segment offset (r*32 + l), so each load and
-// store instruction of a warp covers 512 contiguous bytes. Scans run in registers: within the pack, across lanes
-// (shfl_up), across rounds (running segment total), across the 8 warps (shared memory), then across tiles.
+// One block per tile (tile = blockIdx.x; blocks are dispatched in index order, so every predecessor a tile waits for
+// is resident or finished). A tile is 256 threads x ROUNDS 16-byte packs held in registers: 48 KB (12 rounds) for
+// 4-byte and 64 KB (16 rounds) for 8-byte types, the largest tiles that keep 3 / 2 blocks resident per SM; larger
+// tiles mean fewer look-backs per byte. Warp w owns a contiguous segment; in round r lane l holds the pack at segment
+// offset (r*32 + l), so every load and store instruction of a warp covers 512 contiguous bytes. Scans run in
+// registers: within the pack, across lanes (shfl_up), across rounds (running segment total), across the 8 warps
+// (shared memory), then across tiles. Unaligned input or output uses the same kernel with per-element loads.
 //
-// Cross-tile protocol: a tile takes its index from an atomic ticket (so every tile it waits on belongs to a block that
-// is already running), publishes its aggregate (flag A), looks back over windows of 32 predecessors with one lane per
-// predecessor until it meets an inclusive prefix (flag P), then publishes its own inclusive prefix. Status words
-// carry the call's epoch, so the scratch needs no clearing between calls on a stream: the block that takes the last
-// ticket resets the ticket and advances the epoch. 4-byte types pack flag, epoch and value in one 64-bit word
-// (relaxed 64-bit loads/stores are single-copy atomic); 8-byte types keep values in separate aggregate/prefix slots
-// published with a release store of the flag word and read after an acquire load of it.
-// Every spin is bounded by %globaltimer; on timeout the tile raises the device error word and an abort mark that
-// stops the other tiles' waits of the same call.
+// Cross-tile protocol: a tile publishes its aggregate (flag A), then the WHOLE block looks back: thread i polls the
+// predecessors at distance i, i + 256, ... so one L2 round trip covers a window of kLookSpan tiles, more than a
+// launch keeps in flight. The window is complete as soon as every predecessor up to the nearest inclusive prefix
+// (flag P) is valid; the tile then publishes its own inclusive prefix. Status words carry an epoch handed out by the
+// host per call on the stream's cached scratch (a caller buffer is cleared and uses epoch 1), so the scratch needs no
+// clearing between calls. A status is one 64-bit word per 32 bits of value: flag (2 bits) | epoch (30 bits) | 32
+// value bits; relaxed 64-bit accesses are single-copy atomic, and an 8-byte value's two words are accepted only when
+// both carry the same flag and epoch. Every spin is bounded by %globaltimer; on timeout the block raises the device
+// error word and an abort mark that ends the other blocks' waits of the same call.
 #include <type_traits>
 
 #include "common.cuh"
@@ -28,26 +31,36 @@ namespace a3b
     {
         constexpr int kBlock = 256;
         constexpr int kWarps = kBlock / 32;
-        constexpr int kRounds = 4;
+#ifndef A3B_SCAN_LOOKSPAN
+#define A3B_SCAN_LOOKSPAN 512
+#endif
+        constexpr int kLookSpan = A3B_SCAN_LOOKSPAN; // predecessors polled per look-back window (multiple of 256)
         constexpr unsigned kEpochMask = 0x3FFFFFFFu;
         constexpr unsigned kFlagA = 1u, kFlagP = 2u;
 
         struct ScanHeader
         {
-            unsigned ticket;
-            unsigned epoch;
-            unsigned abortEpoch;
-            unsigned pad[13];
+            unsigned abortEpoch; // epoch of a call whose waits gave up
+            unsigned pad[15];
         };
         static_assert(sizeof(ScanHeader) == 64, "header size");
+
+        // Tile shape per element size (measured on B200): 48 KB tiles for 4-byte and 64 KB tiles for 8-byte types
+        // (12 / 16 rounds of one 16-byte pack per thread), the largest that keep 3 / 2 blocks resident per SM.
+        template<int ES>
+        constexpr int roundsFor()
+        {
+            return ES == 4 ? 12 : 16;
+        }
 
         template<typename T>
         struct Traits
         {
-            static constexpr int W = 16 / static_cast<int>(sizeof(T));
-            static constexpr int ITEMS = W * kRounds;
-            static constexpr int TILE = kBlock * ITEMS;
-            using Bits = std::conditional_t<sizeof(T) == 4, uint32_t, uint64_t>;
+            static constexpr int W = 16 / static_cast<int>(sizeof(T));    // elements per 16-byte pack
+            static constexpr int ROUNDS = roundsFor<sizeof(T)>();         // packs per thread
+            static constexpr int TILE = kBlock * ROUNDS * W;              // elements per tile
+            static constexpr int WORDS = static_cast<int>(sizeof(T)) / 4; // 64-bit status words per tile
+            static constexpr int MIN_BLOCKS = ROUNDS <= 8 ? 4 : (ROUNDS <= 12 ? 3 : 2);
         };
 
         template<typename T>
@@ -61,96 +74,54 @@ namespace a3b
                 return static_cast<T>(static_cast<std::make_unsigned_t<T>>(a) + static_cast<std::make_unsigned_t<T>>(b));
         }
 
-        template<typename T>
-        __device__ __forceinline__ typename Traits<T>::Bits toBits(T v)
-        {
-            typename Traits<T>::Bits b;
-            memcpy(&b, &v, sizeof(T));
-            return b;
-        }
-
-        template<typename T>
-        __device__ __forceinline__ T fromBits(typename Traits<T>::Bits b)
-        {
-            T v;
-            memcpy(&v, &b, sizeof(T));
-            return v;
-        }
-
         __host__ __device__ inline size_t align256(size_t x)
         {
             return (x + 255u) & ~size_t{255u};
         }
 
-        // scratch layout: header | 4-byte T: u64 status[tiles] | 8-byte T: u32 flags[tiles], u64 agg[tiles], u64 pre[tiles]
-        template<typename T>
-        __host__ __device__ inline size_t scratchBytes(uint64_t tiles)
+        // scratch layout: header | u64 status[tiles * WORDS]
+        __host__ __device__ inline size_t scratchBytes(uint64_t tiles, int words)
         {
-            if constexpr(sizeof(T) == 4)
-                return sizeof(ScanHeader) + align256(tiles * 8u);
-            else
-                return sizeof(ScanHeader) + align256(tiles * 4u) + 2u * align256(tiles * 8u);
+            return sizeof(ScanHeader) + align256(tiles * 8u * static_cast<uint64_t>(words));
         }
 
         template<typename T>
-        struct StatusView
+        struct Status
         {
-            uint64_t* word;   // 4-byte T
-            unsigned* flags;  // 8-byte T
-            uint64_t* agg;
-            uint64_t* pre;
-
-            __device__ static StatusView make(ScanHeader* hdr, uint64_t tiles)
-            {
-                StatusView v{};
-                char* base = reinterpret_cast<char*>(hdr + 1);
-                if constexpr(sizeof(T) == 4)
-                    v.word = reinterpret_cast<uint64_t*>(base);
-                else
-                {
-                    v.flags = reinterpret_cast<unsigned*>(base);
-                    v.agg = reinterpret_cast<uint64_t*>(base + align256(tiles * 4u));
-                    v.pre = reinterpret_cast<uint64_t*>(base + align256(tiles * 4u) + align256(tiles * 8u));
-                }
-                return v;
-            }
+            uint64_t* word;
 
             __device__ void publish(uint64_t tile, unsigned flag, unsigned epoch, T value) const
             {
-                if constexpr(sizeof(T) == 4)
-                {
-                    uint64_t const w = (static_cast<uint64_t>(flag) << 62) | (static_cast<uint64_t>(epoch) << 32)
-                                       | static_cast<uint64_t>(toBits(value));
-                    stRelaxedU64(word + tile, w);
-                }
-                else
-                {
-                    stRelaxedU64((flag == kFlagA ? agg : pre) + tile, toBits(value));
-                    stReleaseU32(flags + tile, (flag << 30) | epoch);
-                }
+                constexpr int WD = Traits<T>::WORDS;
+                uint32_t parts[WD];
+                memcpy(parts, &value, sizeof(T));
+                uint64_t const tag = (static_cast<uint64_t>(flag) << 62) | (static_cast<uint64_t>(epoch) << 32);
+#pragma unroll
+                for(int k = 0; k < WD; ++k)
+                    stRelaxedU64(word + tile * WD + k, tag | parts[k]);
             }
 
-            // returns the flag seen for `tile` in this epoch (0 = not yet) and its value
+            // flag seen for `tile` in this epoch (0 = not yet, or the words of an 8-byte value disagree) and its value
             __device__ unsigned peek(uint64_t tile, unsigned epoch, T& value) const
             {
-                if constexpr(sizeof(T) == 4)
+                constexpr int WD = Traits<T>::WORDS;
+                uint64_t w[WD];
+#pragma unroll
+                for(int k = 0; k < WD; ++k)
+                    w[k] = ldRelaxedU64(word + tile * WD + k);
+                unsigned const tag = static_cast<unsigned>(w[0] >> 32);
+                if((tag & kEpochMask) != epoch)
+                    return 0u;
+                uint32_t parts[WD];
+#pragma unroll
+                for(int k = 0; k < WD; ++k)
                 {
-                    uint64_t const w = ldRelaxedU64(word + tile);
-                    unsigned const e = static_cast<unsigned>(w >> 32) & kEpochMask;
-                    if(e != epoch)
+                    if(static_cast<unsigned>(w[k] >> 32) != tag)
                         return 0u;
-                    value = fromBits<T>(static_cast<uint32_t>(w));
-                    return static_cast<unsigned>(w >> 62);
+                    parts[k] = static_cast<uint32_t>(w[k]);
                 }
-                else
-                {
-                    unsigned const f = ldAcquireU32(flags + tile);
-                    if((f & kEpochMask) != epoch)
-                        return 0u;
-                    unsigned const flag = f >> 30;
-                    value = fromBits<T>(ldRelaxedU64((flag == kFlagA ? agg : pre) + tile));
-                    return flag;
-                }
+                memcpy(&value, parts, sizeof(T));
+                return tag >> 30;
             }
         };
 
@@ -164,53 +135,186 @@ namespace a3b
             return v;
         }
 
+        template<typename T>
+        struct Shared
+        {
+            T warpTotal[kWarps];
+            T red[kWarps];
+            int firstP[kLookSpan / 32];
+            int firstInv[kLookSpan / 32];
+            int abort;
+        };
+
+        // Block-wide look-back for `tile` (> 0) whose aggregate is already published; returns the exclusive prefix.
+        // One window covers kLookSpan predecessors: thread i polls predecessors at distance i, i + 256, ... so a
+        // single L2 round trip spans more tiles than a launch keeps in flight (the distance to the nearest published
+        // inclusive prefix stays inside one window). A window is complete as soon as every predecessor up to the
+        // nearest inclusive prefix is valid (stragglers farther back do not matter); without a prefix in the window
+        // all of it must be valid and the window moves back. Sets sh.abort (and the error word) when a wait gives up.
+        template<typename T>
+        __device__ T lookBack(
+            Status<T> const& st,
+            uint64_t tile,
+            unsigned epoch,
+            Shared<T>& sh,
+            ScanHeader* hdr,
+            unsigned* errWord,
+            uint64_t timeoutNs)
+        {
+            constexpr int Q = kLookSpan / kBlock;
+            int const warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+            uint64_t const t0 = globalTimerNs();
+            int64_t pred = static_cast<int64_t>(tile) - 1;
+            T acc = T(0);
+            int polls = 0;
+            while(true)
+            {
+                T val[Q];
+                unsigned flag[Q];
+                int64_t j[Q];
+#pragma unroll
+                for(int q = 0; q < Q; ++q)
+                {
+                    j[q] = pred - static_cast<int64_t>(threadIdx.x) - q * kBlock;
+                    val[q] = T(0);
+                    flag[q] = j[q] >= 0 ? 0u : kFlagP; // before tile 0: an empty inclusive prefix
+                }
+                int stop;
+                while(true)
+                {
+#pragma unroll
+                    for(int q = 0; q < Q; ++q)
+                        if(flag[q] == 0u)
+                            flag[q] = st.peek(static_cast<uint64_t>(j[q]), epoch, val[q]);
+#pragma unroll
+                    for(int q = 0; q < Q; ++q)
+                    {
+                        unsigned const pm = __ballot_sync(0xffffffffu, flag[q] == kFlagP);
+                        unsigned const im = __ballot_sync(0xffffffffu, flag[q] == 0u);
+                        if(lane == 0)
+                        {
+                            sh.firstP[q * kWarps + warp] = pm ? __ffs(pm) - 1 : 32;
+                            sh.firstInv[q * kWarps + warp] = im ? __ffs(im) - 1 : 32;
+                        }
+                    }
+                    __syncthreads();
+                    // distance d = q*256 + w*32 + lane: scan (q, w) from the far end so the last hit is the nearest
+                    stop = kLookSpan;
+                    int inv = kLookSpan;
+#pragma unroll
+                    for(int k = Q * kWarps - 1; k >= 0; --k)
+                    {
+                        if(sh.firstP[k] < 32)
+                            stop = k * 32 + sh.firstP[k];
+                        if(sh.firstInv[k] < 32)
+                            inv = k * 32 + sh.firstInv[k];
+                    }
+                    if(stop < kLookSpan ? inv > stop : inv == kLookSpan)
+                        break;
+                    if(threadIdx.x == 0 && (++polls & 7) == 0)
+                        sh.abort = (globalTimerNs() - t0 > timeoutNs) || (ldRelaxedU32(&hdr->abortEpoch) == epoch);
+                    __syncthreads(); // firstP / firstInv are rewritten by the next poll
+                    if(sh.abort)
+                        break;
+                    if(polls > 4)
+                        __nanosleep(32);
+                }
+                if(sh.abort)
+                    break;
+                T mine = T(0);
+#pragma unroll
+                for(int q = 0; q < Q; ++q)
+                    if(q * kBlock + static_cast<int>(threadIdx.x) <= stop && j[q] >= 0)
+                        mine = add(mine, val[q]);
+                T const ws = warpSum(mine);
+                if(lane == 0)
+                    sh.red[warp] = ws;
+                __syncthreads();
+                T window = T(0);
+#pragma unroll
+                for(int w = 0; w < kWarps; ++w)
+                    window = add(window, sh.red[w]);
+                acc = add(window, acc);
+                __syncthreads(); // firstP / red are rewritten by the next window
+                if(stop < kLookSpan)
+                    break;
+                pred -= kLookSpan;
+            }
+            if(sh.abort && threadIdx.x == 0)
+            {
+                atomicOr(errWord, kErrTimeout);
+                stRelaxedU32(&hdr->abortEpoch, epoch);
+            }
+            return acc;
+        }
+
+        // Scan of one warp-segment round in place: p holds one 16-byte pack per lane; `run` is the segment total so
+        // far (uniform in the warp) and is advanced by the round total.
+        template<typename T, bool INCL>
+        __device__ __forceinline__ void scanRound(T (&p)[Traits<T>::W], T& run)
+        {
+            constexpr int W = Traits<T>::W;
+            int const lane = threadIdx.x & 31;
+            T incl[W];
+            incl[0] = p[0];
+#pragma unroll
+            for(int k = 1; k < W; ++k)
+                incl[k] = add(incl[k - 1], p[k]);
+            T x = incl[W - 1];
+#pragma unroll
+            for(int d = 1; d < 32; d <<= 1)
+            {
+                T const y = __shfl_up_sync(0xffffffffu, x, d);
+                if(lane >= d)
+                    x = add(y, x);
+            }
+            T laneExcl = __shfl_up_sync(0xffffffffu, x, 1);
+            if(lane == 0)
+                laneExcl = T(0);
+            T const roundTotal = __shfl_sync(0xffffffffu, x, 31);
+            T const pre = add(run, laneExcl);
+            if constexpr(INCL)
+            {
+#pragma unroll
+                for(int k = 0; k < W; ++k)
+                    p[k] = add(pre, incl[k]);
+            }
+            else
+            {
+                p[0] = pre;
+#pragma unroll
+                for(int k = 1; k < W; ++k)
+                    p[k] = add(pre, incl[k - 1]);
+            }
+            run = add(run, roundTotal);
+        }
+
+        // ---------------------------------------------------------------- one tile per block, data in registers
+        // Tile = blockIdx.x: blocks are dispatched in index order, so every predecessor a block waits for is already
+        // resident (the bounded waits turn any violation into a reported timeout, never a hang).
         template<typename T, bool INCL, bool VEC>
-        __global__ void __launch_bounds__(kBlock) scanKernel(
+        __global__ void __launch_bounds__(kBlock, Traits<T>::MIN_BLOCKS) scanTileKernel(
             T const* in,
             T* out,
             uint64_t n,
-            uint64_t tiles,
             T const* carryIn,
             ScanHeader* hdr,
+            unsigned epoch,
             unsigned* errWord,
             uint64_t timeoutNs,
             uint64_t stallTile)
         {
             using Tr = Traits<T>;
             constexpr int W = Tr::W;
-            __shared__ uint64_t sTile;
-            __shared__ unsigned sEpoch;
-            __shared__ T sWarpTotal[kWarps];
-            __shared__ T sWarpPrefix[kWarps];
-            __shared__ T sTilePrefix;
-
+            __shared__ Shared<T> sh;
             int const warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-
+            uint64_t const tile = blockIdx.x;
             if(threadIdx.x == 0)
-            {
-                unsigned const e = ldRelaxedU32(&hdr->epoch);
-                __threadfence(); // the epoch read precedes the ticket claim
-                unsigned const t = atomicAdd(&hdr->ticket, 1u);
-                unsigned cur = (e + 1u) & kEpochMask;
-                if(cur == 0u)
-                    cur = 1u;
-                if(t == tiles - 1u)
-                {
-                    // every other block has claimed (and so has read the epoch): reset for the next call
-                    __threadfence();
-                    stRelaxedU32(&hdr->ticket, 0u);
-                    stRelaxedU32(&hdr->epoch, cur);
-                }
-                sTile = t;
-                sEpoch = cur;
-            }
-            __syncthreads();
-            uint64_t const tile = sTile;
-            unsigned const epoch = sEpoch;
-            StatusView<T> const st = StatusView<T>::make(hdr, tiles);
+                sh.abort = 0;
+            Status<T> const st{reinterpret_cast<uint64_t*>(hdr + 1)};
 
-            // ---- load: warp segment of 32*ITEMS elements, round r / lane l -> pack (r*32 + l)
-            uint64_t const segBase = tile * Tr::TILE + static_cast<uint64_t>(warp) * (32 * Tr::ITEMS);
+            constexpr int kRounds = Tr::ROUNDS;
+            uint64_t const segBase = tile * Tr::TILE + static_cast<uint64_t>(warp) * (32 * kRounds * W);
             bool const full = (tile + 1u) * Tr::TILE <= n;
             T v[kRounds][W];
             if(VEC && full)
@@ -233,135 +337,38 @@ namespace a3b
                         v[r][k] = idx < n ? in[idx] : T(0);
                     }
             }
-
-            // ---- scan inside the warp segment (values become segment-relative exclusive/inclusive prefixes)
             T run = T(0);
 #pragma unroll
             for(int r = 0; r < kRounds; ++r)
-            {
-                T incl[W];
-                incl[0] = v[r][0];
-#pragma unroll
-                for(int k = 1; k < W; ++k)
-                    incl[k] = add(incl[k - 1], v[r][k]);
-                T x = incl[W - 1];
-#pragma unroll
-                for(int d = 1; d < 32; d <<= 1)
-                {
-                    T const y = __shfl_up_sync(0xffffffffu, x, d);
-                    if(lane >= d)
-                        x = add(y, x);
-                }
-                T laneExcl = __shfl_up_sync(0xffffffffu, x, 1);
-                if(lane == 0)
-                    laneExcl = T(0);
-                T const roundTotal = __shfl_sync(0xffffffffu, x, 31);
-                T const pre = add(run, laneExcl);
-                if constexpr(INCL)
-                {
-#pragma unroll
-                    for(int k = 0; k < W; ++k)
-                        v[r][k] = add(pre, incl[k]);
-                }
-                else
-                {
-                    v[r][0] = pre;
-#pragma unroll
-                    for(int k = 1; k < W; ++k)
-                        v[r][k] = add(pre, incl[k - 1]);
-                }
-                run = add(run, roundTotal);
-            }
+                scanRound<T, INCL>(v[r], run);
             if(lane == 0)
-                sWarpTotal[warp] = run;
+                sh.warpTotal[warp] = run;
             __syncthreads();
-
-            // ---- tile aggregate, warp prefixes, look-back (warp 0)
-            if(warp == 0)
-            {
-                T x = lane < kWarps ? sWarpTotal[lane] : T(0);
+            T warpPrefix = T(0), agg = T(0);
 #pragma unroll
-                for(int d = 1; d < kWarps; d <<= 1)
-                {
-                    T const y = __shfl_up_sync(0xffffffffu, x, d);
-                    if(lane >= d)
-                        x = add(y, x);
-                }
-                T wEx = __shfl_up_sync(0xffffffffu, x, 1);
-                if(lane == 0)
-                    wEx = T(0);
-                if(lane < kWarps)
-                    sWarpPrefix[lane] = wEx;
-                T const tileAgg = __shfl_sync(0xffffffffu, x, kWarps - 1);
-                bool const stalled = (tile == stallTile);
-
-                T prefix = T(0);
-                if(tile == 0)
-                {
-                    if(carryIn)
-                        prefix = *carryIn;
-                }
-                else
-                {
-                    if(lane == 0 && !stalled)
-                        st.publish(tile, kFlagA, epoch, tileAgg);
-                    uint64_t const t0 = globalTimerNs();
-                    bool gaveUp = false;
-                    int64_t pred = static_cast<int64_t>(tile) - 1;
-                    T acc = T(0);
-                    while(true)
-                    {
-                        int64_t const j = pred - lane;
-                        T val = T(0);
-                        unsigned flag = kFlagP; // lanes before tile 0 count as an (empty) inclusive prefix
-                        int spins = 0;
-                        while(true)
-                        {
-                            if(j >= 0)
-                                flag = st.peek(static_cast<uint64_t>(j), epoch, val);
-                            if(__all_sync(0xffffffffu, flag != 0u))
-                                break;
-                            ++spins;
-                            if(spins > 8)
-                                __nanosleep(spins > 64 ? 256 : 32);
-                            bool timedOut = false;
-                            if(lane == 0)
-                                timedOut = (globalTimerNs() - t0 > timeoutNs)
-                                           || (ldRelaxedU32(&hdr->abortEpoch) == epoch);
-                            if(__shfl_sync(0xffffffffu, timedOut, 0))
-                            {
-                                gaveUp = true;
-                                break;
-                            }
-                        }
-                        if(gaveUp)
-                            break;
-                        unsigned const pmask = __ballot_sync(0xffffffffu, flag == kFlagP);
-                        int const stop = __ffs(pmask) - 1; // nearest predecessor holding an inclusive prefix
-                        T const mine = (pmask == 0u || lane <= stop) && j >= 0 ? val : T(0);
-                        acc = add(warpSum(mine), acc);
-                        if(pmask != 0u)
-                            break;
-                        pred -= 32;
-                    }
-                    if(gaveUp && lane == 0)
-                    {
-                        atomicOr(errWord, kErrTimeout);
-                        stRelaxedU32(&hdr->abortEpoch, epoch);
-                    }
-                    prefix = acc;
-                }
-                if(lane == 0)
-                {
-                    if(!stalled)
-                        st.publish(tile, kFlagP, epoch, add(prefix, tileAgg));
-                    sTilePrefix = prefix;
-                }
+            for(int w = 0; w < kWarps; ++w)
+            {
+                T const t = sh.warpTotal[w];
+                if(w < warp)
+                    warpPrefix = add(warpPrefix, t);
+                agg = add(agg, t);
             }
-            __syncthreads();
-
-            // ---- add tile and warp offsets, store
-            T const off = add(sTilePrefix, sWarpPrefix[warp]);
+            bool const stalled = (tile == stallTile);
+            T prefix = T(0);
+            if(tile == 0)
+            {
+                if(carryIn)
+                    prefix = *carryIn;
+            }
+            else
+            {
+                if(threadIdx.x == 0 && !stalled)
+                    st.publish(tile, kFlagA, epoch, agg);
+                prefix = lookBack<T>(st, tile, epoch, sh, hdr, errWord, timeoutNs);
+            }
+            if(threadIdx.x == 0 && !stalled)
+                st.publish(tile, kFlagP, epoch, add(prefix, agg));
+            T const off = add(prefix, warpPrefix);
             if(VEC && full)
             {
 #pragma unroll
@@ -415,13 +422,14 @@ namespace a3b
             if(rc)
                 return rc;
             uint64_t const tiles = tilesFor<T>(n);
-            if(tiles >= 0xFFFFFFFFull)
+            if(tiles >= 0x7FFFFFFFull)
             {
                 setError("scan of %llu elements exceeds the tile index range", static_cast<unsigned long long>(n));
                 return A3B_ERR_TOO_LARGE;
             }
-            size_t const need = scratchBytes<T>(tiles);
+            size_t const need = scratchBytes(tiles, Traits<T>::WORDS);
             void* scr = nullptr;
+            unsigned epoch = 1u;
             if(buffer)
             {
                 if(bufBytes < need)
@@ -429,21 +437,21 @@ namespace a3b
                     setError("scan buffer too small: %zu bytes given, %zu needed", bufBytes, need);
                     return A3B_ERR_INVALID;
                 }
-                A3B_CUDA(cudaMemsetAsync(buffer, 0, need, s));
+                A3B_CUDA(cudaMemsetAsync(buffer, 0, need, s)); // caller memory: cleared, then epoch 1
                 scr = buffer;
             }
             else
             {
-                rc = streamScratch(s, kScratchScan, need, &scr);
+                rc = streamScratch(s, kScratchScan, need, &scr, &epoch);
                 if(rc)
                     return rc;
             }
             auto* hdr = static_cast<ScanHeader*>(scr);
-            bool const vec = aligned16(in) && aligned16(out);
             uint64_t const to = waitTimeoutNs();
+            bool const vec = aligned16(in) && aligned16(out);
             dim3 const grid(static_cast<unsigned>(tiles));
 #define A3B_SCAN_LAUNCH(INCL, VEC)                                                                                    \
-    scanKernel<T, INCL, VEC><<<grid, kBlock, 0, s>>>(in, out, n, tiles, carry, hdr, props->errWord, to, stallTile)
+    scanTileKernel<T, INCL, VEC><<<grid, kBlock, 0, s>>>(in, out, n, carry, hdr, epoch, props->errWord, to, stallTile)
             if(inclusive)
             {
                 if(vec)
@@ -507,9 +515,9 @@ extern "C"
         int const es = dtypeSize(dtype);
         if(es == 0)
             return 0;
-        uint64_t const tile = static_cast<uint64_t>(kBlock) * kRounds * (16 / es);
+        uint64_t const tile = es == 4 ? Traits<uint32_t>::TILE : Traits<uint64_t>::TILE;
         uint64_t const tiles = (n + tile - 1) / tile;
-        return es == 4 ? scratchBytes<uint32_t>(tiles) : scratchBytes<uint64_t>(tiles);
+        return scratchBytes(tiles, es / 4);
     }
 
     int a3b_scan(a3b_stream_t stream, int dtype, int inclusive, void const* in, void* out, uint64_t n,

@@ -102,8 +102,9 @@ def pci_bus_id(torch, ordinal):
 
 
 # ------------------------------------------------------------------------------------------------ device timing
-def time_steps(torch, dist_on, step, steps, warmup, kernel_events=None):
-    """W untimed steps, then K steps between barrier+sync on both sides; returns (ms per step, kernel ms avg)."""
+def time_steps(torch, dist_on, step, steps, warmup, kernel_events=True):
+    """W untimed steps, then K steps between barrier+sync on both sides; returns (ms per step, average ms between
+    the per-step kernel events that `step` records, or None when kernel_events is False)."""
     for _ in range(warmup):
         step(None)
     torch.cuda.synchronize()
@@ -124,7 +125,7 @@ def time_steps(torch, dist_on, step, steps, warmup, kernel_events=None):
         import torch.distributed as dist
         dist.barrier()
     total = t0.elapsed_time(t1)
-    kern = statistics.mean(a.elapsed_time(b) for a, b in ev)
+    kern = statistics.mean(a.elapsed_time(b) for a, b in ev) if kernel_events else None
     return total / steps, kern
 
 
@@ -204,7 +205,7 @@ def run_b200(args):
                       src.element_size(), sh)
 
         e_steps = max(1, min(args.steps, 10))
-        e_ms, _ = time_steps(torch, dist_on, e2e_step, e_steps, 1)
+        e_ms, _ = time_steps(torch, dist_on, e2e_step, e_steps, 1, kernel_events=False)
         e_ms = max_over_ranks(torch, dist_on, e_ms)
         e2e = {"value": total_bytes / (e_ms * 1e-3) / 1e9, "unit": "GB/s", "h2d_bytes_per_step": 4 * N_SUMSQ,
                "d2h_bytes_per_step": (8 if dist_on else 4) * world, "steps": e_steps,
@@ -367,6 +368,59 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
+def run_profile_case(args):
+    """One kernel at a chosen size, W + K launches, for ncu captures (`-k regex:<kernel>`); not a bench line."""
+    import torch
+    from alpaka3_b200 import algo
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    case, lg = args.profile_case, args.log2n
+    if case == "sumsq":
+        n = 1 << (lg or 28)
+        x = torch.empty(n, dtype=torch.float32, device=dev)
+        algo.random_f32(x, SEED, -1.0, 1.0)
+        out = torch.empty(1, dtype=torch.float32, device=dev)
+        fn, nbytes = (lambda: algo.transform_reduce(0.0, out, "plus", "square", x)), 4 * n
+    elif case in ("triad", "copy", "dot"):
+        n = 1 << (lg or 25)
+        a, b, c = (torch.empty(n, dtype=torch.float64, device=dev) for _ in range(3))
+        algo.babelstream("init", a, b, c)
+        out = torch.empty(1, dtype=torch.float64, device=dev)
+        if case == "dot":
+            fn, nbytes = (lambda: algo.transform_reduce(0.0, out, "plus", "product", a, b)), 16 * n
+        else:
+            fn, nbytes = (lambda: algo.babelstream(case, a, b, c)), (24 if case == "triad" else 16) * n
+    elif case == "scan_i32":
+        n = 1 << (lg or 28)
+        x = torch.empty(n, dtype=torch.int32, device=dev)
+        algo.random_u32(x, SEED, shift=28)
+        y = torch.empty_like(x)
+        fn, nbytes = (lambda: algo.exclusive_scan(y, x)), 8 * n
+    elif case == "scan_u64":
+        n = 1 << (lg or 27)
+        x = torch.empty(n, dtype=torch.int64, device=dev)
+        algo.random_u64(x, SEED)
+        y = torch.empty_like(x)
+        fn, nbytes = (lambda: algo.inclusive_scan(y, x)), 16 * n
+    elif case == "nbody":
+        n = 1 << (lg or 16)
+        m, px, py, pz = (torch.empty(n, dtype=torch.float32, device=dev) for _ in range(4))
+        algo.random_f32(m, SEED + 1, 0.5, 1.0)
+        for k, t in enumerate((px, py, pz)):
+            algo.random_f32(t, SEED + 2 + k, 0.0, 1.0)
+        v = [torch.zeros(n, dtype=torch.float32, device=dev) for _ in range(3)]
+        fn, nbytes = (lambda: algo.nbody_step(m, px, py, pz, *v, 1e-3, 1e-3)), 20 * n * n
+    else:
+        side = 1 << ((lg or 26) // 2)
+        u = torch.empty((side + 2, side + 2), dtype=torch.float64, device=dev)
+        dx = 1.0 / (side + 1)
+        algo.heat_init(u, dx, dx)
+        w = u.clone()
+        fn, nbytes = (lambda: algo.heat_step(u, w, 0.2, 0.2)), 16 * side * side
+    ms, kern = time_steps(torch, False, lambda ev: _wrap(torch, ev, fn), args.steps, args.warmup)
+    print(json.dumps({"profile_case": case, "n_log2": lg, "kernel_ms": kern, "units_per_s": nbytes / (kern * 1e-3)}))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -377,11 +431,17 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=8.0)
+    ap.add_argument("--profile-case", default=None,
+                    choices=["sumsq", "triad", "copy", "dot", "scan_i32", "scan_u64", "nbody", "heat"],
+                    help="run only this kernel (for ncu captures of a small case); prints a short line")
+    ap.add_argument("--log2n", type=int, default=None, help="problem size (log2 elements) for --profile-case")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":
         run_reference(args)
+    elif args.profile_case:
+        run_profile_case(args)
     else:
         run_b200(args)
 

@@ -123,7 +123,7 @@ def test_lookback_timeout_reports_error(cuda):
     capi.device_error(s, clear=True)
     capi.call("a3b_set_wait_timeout_ns", 20_000_000)  # 20 ms
     try:
-        n = 4096 * 6
+        n = 1 << 18  # at least 8 tiles for every tile size; tile 2 stalls
         x = torch.ones(n, dtype=torch.int32, device=cuda)
         out = torch.empty_like(x)
         capi.call("a3b_scan_debug_stall", s, capi.I32, ctypes.c_void_p(x.data_ptr()), ctypes.c_void_p(out.data_ptr()),
