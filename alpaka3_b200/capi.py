@@ -53,6 +53,7 @@ SIGNATURES = {
     "a3b_random_f32": [_P, _P, _U64, _U64, _U64, _F, _F],
     "a3b_transform_reduce": [_P, _I, _I, _I, _P, _P, _U64, _P, _P],
     "a3b_transform_reduce_partial": [_P, _I, _I, _I, _P, _P, _U64, _P, _P],
+    "a3b_transform_reduce_noalloc": [_P, _I, _I, _I, _P, _P, _U64, _P, _P],
     "a3b_reduce_2d": [_P, _I, _I, _P, _U64, _U64, _U64, _P, _P],
     "a3b_scan_buffer_size": [_I, _U64],
     "a3b_scan": [_P, _I, _I, _P, _P, _U64, _P, _P, ctypes.c_size_t],

@@ -15,6 +15,7 @@
 // The result depends only on (device SM count, n): repeated runs give identical bits.
 #include <cfloat>
 #include <climits>
+#include <mutex>
 #include <type_traits>
 
 #include "common.cuh"
@@ -498,6 +499,136 @@ namespace a3b
     } // namespace
 } // namespace a3b
 
+namespace a3b
+{
+    namespace
+    {
+        // ------------------------------------------------------------------------------------------------------
+        // Variant for callers that cannot allocate device memory: processes whose device memory is owned by another
+        // allocator's pool (a framework that reserves the GPU's memory up front), services that must keep a fixed,
+        // accounted memory footprint, and latency-critical loops that cannot afford an allocation's implicit
+        // synchronisation. Its scratch (ticket header + one 8-byte partial per block) lives in this fixed static
+        // array, which every device that loads the library holds until the process exits.
+        constexpr size_t kNoAllocScratchBytes = 16384; // 64-byte header + up to 2040 block partials
+        __device__ __align__(256) unsigned char g_noAllocScratch[kNoAllocScratchBytes];
+
+        std::mutex gNoAllocMutex;
+        void* gNoAllocAddress[64] = {};
+
+        // Device address of the static scratch for the current device. The array's name is a host-side stand-in,
+        // not a device address, so it is resolved once per device with cudaGetSymbolAddress (this first call must
+        // not happen inside a stream capture).
+        int noAllocScratch(void** ptr)
+        {
+            int dev = 0;
+            A3B_CUDA(cudaGetDevice(&dev));
+            A3B_REQUIRE(dev >= 0 && dev < 64, "device ordinal out of range");
+            std::lock_guard<std::mutex> lock(gNoAllocMutex);
+            if(!gNoAllocAddress[dev])
+            {
+                void* a = nullptr;
+                cudaError_t const e = cudaGetSymbolAddress(&a, g_noAllocScratch);
+                if(e != cudaSuccess)
+                    return cudaFail(e, "cudaGetSymbolAddress(no-allocation scratch)");
+                gNoAllocAddress[dev] = a;
+            }
+            *ptr = gNoAllocAddress[dev];
+            return A3B_OK;
+        }
+
+        template<typename T, int W, int ROp, int XOp>
+        int launchReduceNoAlloc(cudaStream_t s, T const* in0, T const* in1, uint64_t n, T neutral, void* out)
+        {
+            using A = typename AccOf<T, ROp>::type;
+            DeviceProps const* props = nullptr;
+            int rc = currentDevice(&props);
+            if(rc)
+                return rc;
+            int b = 0;
+            A3B_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b, reduceKernel<T, W, ROp, XOp, false>, kBlock, 0));
+            uint64_t const packs = n / W + 1;
+            uint64_t const want = (packs + static_cast<uint64_t>(kBlock) * kUnroll - 1) / (kBlock * kUnroll);
+            uint64_t const full = static_cast<uint64_t>(props->smCount) * static_cast<uint64_t>(b > 0 ? b : 1);
+            uint64_t const grid = want < full ? (want > 0 ? want : 1) : full;
+            size_t const need = sizeof(ReduceScratch) + sizeof(A) * static_cast<size_t>(grid);
+            if(need > kNoAllocScratchBytes)
+            {
+                setError("a3b_transform_reduce_noalloc needs %zu bytes of scratch for %llu blocks on this device, "
+                         "more than its fixed %zu-byte static array",
+                         need, static_cast<unsigned long long>(grid), kNoAllocScratchBytes);
+                return A3B_ERR_TOO_LARGE;
+            }
+            void* scr = nullptr;
+            rc = noAllocScratch(&scr);
+            if(rc)
+                return rc;
+            auto* hdr = static_cast<ReduceScratch*>(scr);
+            // the array keeps the previous call's contents: the block ticket must start at zero
+            A3B_CUDA(cudaMemsetAsync(hdr, 0, sizeof(ReduceScratch), s));
+            auto* partials = reinterpret_cast<A*>(hdr + 1);
+            reduceKernel<T, W, ROp, XOp, false><<<static_cast<unsigned>(grid), kBlock, 0, s>>>(
+                in0, in1, n, n, 0, neutral, out, false, hdr, partials);
+            A3B_CHECK_LAUNCH("transform_reduce_noalloc launch");
+            return A3B_OK;
+        }
+
+        template<typename T, int ROp, int XOp>
+        int noAllocLayout(cudaStream_t s, T const* in0, T const* in1, uint64_t n, T neutral, void* out)
+        {
+            auto al = [&](uintptr_t a)
+            {
+                auto ok = [&](void const* p) { return (reinterpret_cast<uintptr_t>(p) & (a - 1u)) == 0u; };
+                return ok(in0) && (XOp != A3B_XFORM_PRODUCT || ok(in1));
+            };
+            constexpr int W = 16 / sizeof(T);
+            if(al(32))
+                return launchReduceNoAlloc<T, 2 * W, ROp, XOp>(s, in0, in1, n, neutral, out);
+            if(al(16))
+                return launchReduceNoAlloc<T, W, ROp, XOp>(s, in0, in1, n, neutral, out);
+            return launchReduceNoAlloc<T, 1, ROp, XOp>(s, in0, in1, n, neutral, out);
+        }
+
+        template<typename T, int ROp>
+        int noAllocXform(cudaStream_t s, int xop, T const* in0, T const* in1, uint64_t n, T neutral, void* out)
+        {
+            switch(xop)
+            {
+            case A3B_XFORM_IDENTITY:
+                return noAllocLayout<T, ROp, A3B_XFORM_IDENTITY>(s, in0, in1, n, neutral, out);
+            case A3B_XFORM_SQUARE:
+                return noAllocLayout<T, ROp, A3B_XFORM_SQUARE>(s, in0, in1, n, neutral, out);
+            case A3B_XFORM_PRODUCT:
+                A3B_REQUIRE(in1, "product transform needs two inputs");
+                return noAllocLayout<T, ROp, A3B_XFORM_PRODUCT>(s, in0, in1, n, neutral, out);
+            default:
+                setError("unknown transform op %d", xop);
+                return A3B_ERR_INVALID;
+            }
+        }
+
+        template<typename T>
+        int noAllocReduce(cudaStream_t s, int rop, int xop, void const* in0, void const* in1, uint64_t n,
+                          void const* neutral, void* out)
+        {
+            T const nv = *static_cast<T const*>(neutral);
+            auto i0 = static_cast<T const*>(in0);
+            auto i1 = static_cast<T const*>(in1);
+            switch(rop)
+            {
+            case A3B_REDUCE_PLUS:
+                return noAllocXform<T, A3B_REDUCE_PLUS>(s, xop, i0, i1, n, nv, out);
+            case A3B_REDUCE_MIN:
+                return noAllocXform<T, A3B_REDUCE_MIN>(s, xop, i0, i1, n, nv, out);
+            case A3B_REDUCE_MAX:
+                return noAllocXform<T, A3B_REDUCE_MAX>(s, xop, i0, i1, n, nv, out);
+            default:
+                setError("unknown reduce op %d", rop);
+                return A3B_ERR_INVALID;
+            }
+        }
+    } // namespace
+} // namespace a3b
+
 using namespace a3b;
 
 extern "C"
@@ -523,5 +654,31 @@ extern "C"
         A3B_REQUIRE(rows <= 1 || row_pitch_bytes >= row_len * static_cast<uint64_t>(es), "row pitch smaller than a row");
         return reduceEntry(stream, dtype, reduce_op, A3B_XFORM_IDENTITY, in, nullptr, rows, row_len, row_pitch_bytes,
                            neutral, out, false);
+    }
+
+    int a3b_transform_reduce_noalloc(a3b_stream_t stream, int dtype, int reduce_op, int transform_op, void const* in0,
+                                     void const* in1, uint64_t n, void const* neutral, void* out)
+    {
+        A3B_REQUIRE(out && neutral, "null out/neutral");
+        A3B_REQUIRE(in0 || n == 0, "null input");
+        auto s = static_cast<cudaStream_t>(stream);
+        switch(dtype)
+        {
+        case A3B_I32:
+            return noAllocReduce<int32_t>(s, reduce_op, transform_op, in0, in1, n, neutral, out);
+        case A3B_U32:
+            return noAllocReduce<uint32_t>(s, reduce_op, transform_op, in0, in1, n, neutral, out);
+        case A3B_I64:
+            return noAllocReduce<int64_t>(s, reduce_op, transform_op, in0, in1, n, neutral, out);
+        case A3B_U64:
+            return noAllocReduce<uint64_t>(s, reduce_op, transform_op, in0, in1, n, neutral, out);
+        case A3B_F32:
+            return noAllocReduce<float>(s, reduce_op, transform_op, in0, in1, n, neutral, out);
+        case A3B_F64:
+            return noAllocReduce<double>(s, reduce_op, transform_op, in0, in1, n, neutral, out);
+        default:
+            setError("unknown dtype %d", dtype);
+            return A3B_ERR_INVALID;
+        }
     }
 }

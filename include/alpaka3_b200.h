@@ -166,6 +166,18 @@ A3B_API int a3b_transform_reduce(a3b_stream_t stream, int dtype, int reduce_op, 
 A3B_API int a3b_transform_reduce_partial(a3b_stream_t stream, int dtype, int reduce_op, int transform_op, void const* in0,
                                  void const* in1, uint64_t n, void const* neutral, void* partial_out);
 
+/* No counterpart in the reference: a3b_transform_reduce for callers that cannot allocate device memory -- a process
+ * whose device memory is owned by another allocator's pool, a service that must keep a fixed, accounted memory
+ * footprint, a latency-critical loop that cannot afford an allocation's implicit synchronisation. Same arguments and result
+ * as a3b_transform_reduce over a dense 1-D input; it allocates nothing. Its scratch is one fixed 16 KB static device
+ * array per GPU that loads the library (held until the process exits): a 64-byte header plus one 8-byte partial per
+ * block, i.e. at most 2040 blocks; a device/size that would need more is rejected with A3B_ERR_TOO_LARGE. The first
+ * call on a device looks up that array's device address, so make the first call before any stream capture. All
+ * calls share the array: calls that overlap on the GPU (different streams, devices' own streams in parallel) race
+ * and must be serialised by the caller. */
+A3B_API int a3b_transform_reduce_noalloc(a3b_stream_t stream, int dtype, int reduce_op, int transform_op,
+                                         void const* in0, void const* in1, uint64_t n, void const* neutral, void* out);
+
 /* onHost::reduce(queue, neutral, out, reduceFn, in) (include/alpaka/onHost/algo/reduce.hpp:28-79) over a pitched
  * 2-D view: `rows` rows of `row_len` elements, consecutive rows `row_pitch_bytes` apart (rows = 1 for 1-D data).
  * N-D alpaka buffers whose slower dimensions are dense multiples of the row pitch map onto this form. */
