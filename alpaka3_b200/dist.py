@@ -66,7 +66,10 @@ def scan_carry(total, rank=None, world=None):
     world = dist.get_world_size()
     rank = dist.get_rank()
     gathered = torch.empty(world, dtype=total.dtype, device=total.device)
-    dist.all_gather_into_tensor(gathered, total)
+    if dist.get_backend() == "nccl":
+        dist.all_gather_into_tensor(gathered, total)
+    else:
+        dist.all_gather(list(gathered.chunk(world)), total)
     if rank == 0:
         carry = torch.zeros_like(total)
     else:
@@ -77,7 +80,10 @@ def scan_carry(total, rank=None, world=None):
 def nbody_allgather(full, local):
     """Gather every rank's equal-size shard `local` into `full` (rank-major)."""
     if dist.is_initialized() and dist.get_world_size() > 1:
-        dist.all_gather_into_tensor(full, local)
+        if dist.get_backend() == "nccl":
+            dist.all_gather_into_tensor(full, local)
+        else:
+            dist.all_gather(list(full.chunk(dist.get_world_size())), local)
     else:
         full.copy_(local)
     return full
@@ -98,3 +104,120 @@ def heat_exchange_halos(u, rank, world):
         ops.append(dist.P2POp(dist.irecv, u[rows + 1], rank + 1))
     for req in dist.batch_isend_irecv(ops):
         req.wait()
+
+
+# ------------------------------------------------------------------------------------- sharded algorithms (GPU)
+def _world():
+    if dist.is_initialized():
+        return dist.get_world_size(), dist.get_rank()
+    return 1, 0
+
+
+def transform_reduce(neutral, reduce_fn, transform_fn, in0_local, in1_local=None, out=None):
+    """onHost::transformReduce over data sharded across ranks: one kernel per rank (unrounded 8-byte partial), one
+    all-reduce of the partials, final rounding to the input dtype. Returns a 1-element tensor on every rank."""
+    from . import algo
+    partial = algo.transform_reduce_partial(reduce_fn, transform_fn, in0_local, in1_local, neutral=neutral)
+    allreduce_partial(partial, reduce_fn)
+    res = partial.to(in0_local.dtype)
+    if out is not None:
+        out.copy_(res)
+        return out
+    return res
+
+
+def carry_to_dtype(carry, dtype):
+    """Converts a carry computed as an 8-byte partial (float64, or int64 bits for integers) to the scan's element
+    type; integer carries keep their low bits (two's-complement wrap, as the single-device scan)."""
+    if dtype.is_floating_point:
+        return carry.to(dtype)
+    c = carry.view(torch.int64)
+    if torch.empty(0, dtype=dtype).element_size() == 4:
+        return (c & 0xFFFFFFFF).to(torch.int32).view(dtype)
+    return c.view(dtype)
+
+
+def _scan_sharded(inclusive, out_local, data_local):
+    from . import algo
+    world, rank = _world()
+    carry = None
+    if world > 1:
+        total = algo.transform_reduce_partial("plus", "identity", data_local, neutral=0)
+        if not data_local.dtype.is_floating_point:
+            total = total.view(torch.int64)  # sums of integer shards wrap; int64 bits carry them exactly
+        c, _ = scan_carry(total)
+        carry = carry_to_dtype(c, data_local.dtype)
+    return algo._scan(inclusive, out_local, data_local, None, carry)
+
+
+def exclusive_scan(out_local, data_local):
+    """Exclusive scan of a contiguously sharded array (rank r holds elements [begin_r, end_r)): shard total, all-gather
+    of the totals, scan seeded with the sum of the lower ranks' totals (3N/G traffic per GPU)."""
+    return _scan_sharded(False, out_local, data_local)
+
+
+def inclusive_scan(out_local, data_local):
+    return _scan_sharded(True, out_local, data_local)
+
+
+class NBody:
+    """All-pairs nBody with the bodies split across ranks: every rank keeps all positions (m, x, y, z of n bodies) and
+    the velocities of its own bodies; a step is the local kick + drift followed by an all-gather of the positions."""
+
+    def __init__(self, m, x, y, z, vx_local, vy_local, vz_local, i_begin):
+        self.m, self.x, self.y, self.z = m, x, y, z
+        self.v = (vx_local, vy_local, vz_local)
+        self.i_begin = i_begin
+        self.count = vx_local.numel()
+        self.stage = [torch.empty(self.count, dtype=x.dtype, device=x.device) for _ in range(3)]
+
+    def step(self, dt, eps):
+        from . import algo
+        algo.nbody_step(self.m, self.x, self.y, self.z, *self.v, dt, eps, i_begin=self.i_begin)
+        world, _ = _world()
+        if world > 1:
+            b, e = self.i_begin, self.i_begin + self.count
+            for full, st in zip((self.x, self.y, self.z), self.stage):
+                st.copy_(full[b:e])
+                nbody_allgather(full, st)
+
+
+class HeatSlab:
+    """Row slab of the heat grid on one rank: `rows` interior rows (global rows row_offset+1 ... row_offset+rows) and
+    one ghost row above and below. A step updates the two boundary rows first, sends them to the neighbours (their
+    ghost rows) while the interior rows are updated, and waits for the neighbours' rows before the next step."""
+
+    def __init__(self, cur, nxt, rX, rY):
+        self.cur, self.nxt, self.rX, self.rY = cur, nxt, rX, rY
+        self.rows = cur.shape[0] - 2
+        self.pending = []
+
+    def step(self):
+        from . import algo
+        for r in self.pending:
+            r.wait()
+        self.pending = []
+        world, rank = _world()
+        rows = self.rows
+        if world == 1 or rows < 3:
+            algo.heat_step(self.cur, self.nxt, self.rX, self.rY)
+            if world > 1:
+                heat_exchange_halos(self.nxt, rank, world)
+        else:
+            algo.heat_step(self.cur, self.nxt, self.rX, self.rY, row_begin=1, row_end=2)
+            algo.heat_step(self.cur, self.nxt, self.rX, self.rY, row_begin=rows, row_end=rows + 1)
+            ops = []
+            if rank > 0:
+                ops.append(dist.P2POp(dist.isend, self.nxt[1], rank - 1))
+                ops.append(dist.P2POp(dist.irecv, self.nxt[0], rank - 1))
+            if rank < world - 1:
+                ops.append(dist.P2POp(dist.isend, self.nxt[rows], rank + 1))
+                ops.append(dist.P2POp(dist.irecv, self.nxt[rows + 1], rank + 1))
+            self.pending = dist.batch_isend_irecv(ops)
+            algo.heat_step(self.cur, self.nxt, self.rX, self.rY, row_begin=2, row_end=rows)
+        self.cur, self.nxt = self.nxt, self.cur
+
+    def finish(self):
+        for r in self.pending:
+            r.wait()
+        self.pending = []
