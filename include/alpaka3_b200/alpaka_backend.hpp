@@ -1,0 +1,474 @@
+/* alpaka3 binding of the B200 primitive library (header-only, C++20).
+ *
+ * Include after (or instead of) <alpaka/alpaka.hpp> and link libalpaka3_b200.so. The header adds overloads of
+ *   alpaka::onHost::transformReduce   (alpaka3: include/alpaka/onHost/algo/transformReduce.hpp:59-114)
+ *   alpaka::onHost::reduce            (include/alpaka/onHost/algo/reduce.hpp:28-79)
+ *   alpaka::onHost::exclusiveScan / inclusiveScan / *InPlace   (include/alpaka/onHost/algo/scan.hpp:45-218)
+ * for queues of CUDA devices (Queue<Device<api::Cuda, K>, Q>). Partial ordering picks them over alpaka3's generic
+ * templates because their queue parameter is more specialised. At run time a call goes to the C ABI when
+ *   - the element type is int32/uint32/int64/uint64/float/double,
+ *   - the data are device buffers (IMdSpan) laid out densely, or as rows with one constant pitch,
+ *   - the reduce functor is std::plus or (probed on the host) computes +, min or max, and the transform functor is
+ *     std::identity or computes x, x*x or a*b (probed with scalars, or with Simd<T, 1> for functors such as
+ *     BabelStream's DotMultiplication that take SIMD packs);
+ * every other call is forwarded unchanged to alpaka3's own implementation (onHost::internal::transformReduce /
+ * internal::scan), so the caller's results never depend on the routing. Backend errors throw std::runtime_error, as
+ * alpaka3's ALPAKA_UNIFORM_CUDA_HIP_RT_CHECK does (include/alpaka/core/UniformCudaHip.hpp:42). Blocking queues wait
+ * for the call to finish.
+ */
+#pragma once
+
+#include <alpaka/alpaka.hpp>
+
+#include "../alpaka3_b200.h"
+
+#include <atomic>
+#include <cstdint>
+#include <functional>
+#include <optional>
+#include <stdexcept>
+#include <string>
+#include <type_traits>
+
+namespace alpaka3_b200
+{
+    //! How many calls this process routed to the C ABI / forwarded to alpaka3's own implementation.
+    struct RoutingStats
+    {
+        std::atomic<std::uint64_t> routed{0};
+        std::atomic<std::uint64_t> forwarded{0};
+    };
+
+    inline RoutingStats& routingStats()
+    {
+        static RoutingStats s;
+        return s;
+    }
+
+    namespace detail
+    {
+        inline void check(int rc, char const* what)
+        {
+            if(rc != A3B_OK)
+                throw std::runtime_error(std::string(what) + ": " + a3b_last_error());
+        }
+
+        template<typename T>
+        constexpr int dtypeOf()
+        {
+            if constexpr(std::is_same_v<T, std::int32_t>)
+                return A3B_I32;
+            else if constexpr(std::is_same_v<T, std::uint32_t>)
+                return A3B_U32;
+            else if constexpr(std::is_same_v<T, std::int64_t> || (std::is_same_v<T, long long> && sizeof(T) == 8))
+                return A3B_I64;
+            else if constexpr(std::is_same_v<T, std::uint64_t> || (std::is_same_v<T, unsigned long long> && sizeof(T) == 8))
+                return A3B_U64;
+            else if constexpr(std::is_same_v<T, float>)
+                return A3B_F32;
+            else if constexpr(std::is_same_v<T, double>)
+                return A3B_F64;
+            else
+                return -1;
+        }
+
+        template<typename T, typename R>
+        std::optional<T> scalarOf(R const& r)
+        {
+            if constexpr(std::is_arithmetic_v<std::decay_t<R>>)
+                return static_cast<T>(r);
+            else if constexpr(requires { r[0]; })
+                return static_cast<T>(r[0]);
+            else
+                return std::nullopt;
+        }
+
+        template<typename T, typename>
+        using Pack1 = alpaka::Simd<T, 1u>;
+
+        //! Evaluate a functor on the host with scalar arguments, or with one-lane SIMD packs when it takes packs.
+        template<typename T, typename F, typename... A>
+        std::optional<T> probe(F const& f, A... a)
+        {
+            if constexpr(std::is_invocable_v<F const&, A...>)
+                return scalarOf<T>(f(a...));
+            else if constexpr(std::is_invocable_v<F const&, Pack1<T, A>...>)
+                return scalarOf<T>(f(Pack1<T, A>{static_cast<T>(a)}...));
+            else
+                return std::nullopt;
+        }
+
+        template<typename T, typename F>
+        int reduceOpOf(F const& f)
+        {
+            using D = std::decay_t<F>;
+            if constexpr(std::is_same_v<D, std::plus<>> || std::is_same_v<D, std::plus<T>>)
+                return A3B_REDUCE_PLUS;
+            else
+            {
+                auto const a = probe<T>(f, T(3), T(5)), b = probe<T>(f, T(5), T(3)), c = probe<T>(f, T(7), T(2));
+                if(!a || !b || !c)
+                    return -1;
+                if(*a == T(8) && *b == T(8) && *c == T(9))
+                    return A3B_REDUCE_PLUS;
+                if(*a == T(3) && *b == T(3) && *c == T(2))
+                    return A3B_REDUCE_MIN;
+                if(*a == T(5) && *b == T(5) && *c == T(7))
+                    return A3B_REDUCE_MAX;
+                return -1;
+            }
+        }
+
+        template<typename T, int NIN, typename F>
+        int transformOpOf(F const& f)
+        {
+            using D = std::decay_t<F>;
+            if constexpr(NIN == 1)
+            {
+                if constexpr(std::is_same_v<D, std::identity>)
+                    return A3B_XFORM_IDENTITY;
+                else
+                {
+                    auto const a = probe<T>(f, T(3)), b = probe<T>(f, T(5));
+                    if(!a || !b)
+                        return -1;
+                    if(*a == T(3) && *b == T(5))
+                        return A3B_XFORM_IDENTITY;
+                    if(*a == T(9) && *b == T(25))
+                        return A3B_XFORM_SQUARE;
+                    return -1;
+                }
+            }
+            else if constexpr(NIN == 2)
+            {
+                auto const a = probe<T>(f, T(3), T(5)), b = probe<T>(f, T(7), T(2));
+                if(a && b && *a == T(15) && *b == T(14))
+                    return A3B_XFORM_PRODUCT;
+                return -1;
+            }
+            else
+                return -1;
+        }
+
+        //! Device buffer view as (pointer, rows, row length, row pitch in bytes); false when the layout does not fit.
+        struct Layout
+        {
+            void const* ptr = nullptr;
+            std::uint64_t rows = 0, rowLen = 0, rowPitch = 0;
+
+            bool dense() const
+            {
+                return rows <= 1u || rowPitch == 0u;
+            }
+        };
+
+        template<typename T>
+        bool layoutOf(auto const& view, Layout& out)
+        {
+            auto const ext = alpaka::onHost::getExtents(view);
+            auto const pitch = alpaka::onHost::getPitches(view);
+            constexpr auto dim = std::decay_t<decltype(ext)>::dim();
+            out.ptr = static_cast<void const*>(alpaka::onHost::data(view));
+            if(static_cast<std::uint64_t>(pitch[dim - 1u]) != sizeof(T))
+                return false;
+            std::uint64_t rows = 1u;
+            for(std::uint32_t d = 0; d + 1u < dim; ++d)
+                rows *= static_cast<std::uint64_t>(ext[d]);
+            out.rowLen = static_cast<std::uint64_t>(ext[dim - 1u]);
+            out.rows = rows;
+            if constexpr(dim >= 2u)
+            {
+                // slower dimensions must be dense over rows: pitch[d] == ext[d+1] * pitch[d+1] for d < dim - 2
+                for(std::uint32_t d = 0; d + 2u < dim; ++d)
+                    if(static_cast<std::uint64_t>(pitch[d]) != static_cast<std::uint64_t>(ext[d + 1u]) * pitch[d + 1u])
+                        return false;
+                std::uint64_t const rp = static_cast<std::uint64_t>(pitch[dim - 2u]);
+                out.rowPitch = (rp == out.rowLen * sizeof(T)) ? 0u : rp;
+            }
+            return true;
+        }
+
+        template<typename Q>
+        void* streamOf(Q const& queue)
+        {
+            return reinterpret_cast<void*>(queue.getNativeHandle());
+        }
+
+        template<typename Q>
+        void finish(Q const& queue)
+        {
+            if constexpr(std::is_same_v<ALPAKA_TYPEOF(queue.getQueueKind()), alpaka::queueKind::Blocking>)
+                check(a3b_stream_synchronize(streamOf(queue)), "alpaka3_b200 blocking queue");
+        }
+
+        // Route transformReduce to the C ABI; false when the call is not covered.
+        template<typename T, typename Q>
+        bool tryTransformReduce(
+            Q const& queue,
+            T const& neutral,
+            auto& out,
+            auto const& reduceFn,
+            auto const& transformFn,
+            auto const&... in)
+        {
+            constexpr int NIN = sizeof...(in);
+            constexpr int dt = dtypeOf<T>();
+            if constexpr(dt < 0 || NIN < 1 || NIN > 2)
+                return false;
+            else if constexpr(!(alpaka::concepts::IMdSpan<std::decay_t<decltype(in)>> && ...))
+                return false;
+            else if constexpr(!(std::is_same_v<alpaka::trait::GetValueType_t<std::decay_t<decltype(in)>>, T> && ...))
+                return false;
+            else
+            {
+                int const rop = reduceOpOf<T>(reduceFn);
+                int const xop = transformOpOf<T, NIN>(transformFn);
+                if(rop < 0 || xop < 0)
+                    return false;
+                Layout l[NIN];
+                int k = 0;
+                bool ok = true;
+                ((ok = ok && layoutOf<T>(in, l[k++])), ...);
+                if(!ok)
+                    return false;
+                Layout o;
+                if(!layoutOf<T>(out, o))
+                    return false;
+                void* const s = streamOf(queue);
+                void* const outPtr = const_cast<void*>(o.ptr);
+                if constexpr(NIN == 1)
+                {
+                    if(l[0].dense())
+                        check(a3b_transform_reduce(s, dt, rop, xop, l[0].ptr, nullptr, l[0].rows * l[0].rowLen,
+                                                   &neutral, outPtr),
+                              "alpaka3_b200 transformReduce");
+                    else if(xop == A3B_XFORM_IDENTITY)
+                        check(a3b_reduce_2d(s, dt, rop, l[0].ptr, l[0].rows, l[0].rowLen, l[0].rowPitch, &neutral,
+                                            outPtr),
+                              "alpaka3_b200 reduce");
+                    else
+                        return false;
+                }
+                else
+                {
+                    if(!l[0].dense() || !l[1].dense() || l[0].rows * l[0].rowLen != l[1].rows * l[1].rowLen)
+                        return false;
+                    check(a3b_transform_reduce(s, dt, rop, xop, l[0].ptr, l[1].ptr, l[0].rows * l[0].rowLen,
+                                               &neutral, outPtr),
+                          "alpaka3_b200 transformReduce");
+                }
+                finish(queue);
+                ++routingStats().routed;
+                return true;
+            }
+        }
+
+        // Route a scan to the C ABI; false when the call is not covered.
+        // `buffer` is a pointer to the caller's scan buffer, or nullptr (std::nullptr_t) when the call has none.
+        template<typename Q, typename B>
+        bool tryScan(Q const& queue, bool inclusive, B buffer, auto& out, auto const& in)
+        {
+            using T = alpaka::trait::GetValueType_t<std::decay_t<decltype(in)>>;
+            using TO = alpaka::trait::GetValueType_t<std::decay_t<decltype(out)>>;
+            constexpr int dt = dtypeOf<std::remove_const_t<T>>();
+            if constexpr(dt < 0 || !std::is_same_v<std::remove_const_t<T>, std::remove_const_t<TO>>)
+                return false;
+            else if constexpr(!alpaka::concepts::IMdSpan<std::decay_t<decltype(in)>>)
+                return false;
+            else
+            {
+                Layout li, lo;
+                if(!layoutOf<std::remove_const_t<T>>(in, li) || !layoutOf<std::remove_const_t<T>>(out, lo))
+                    return false;
+                if(!li.dense() || !lo.dense() || li.rows * li.rowLen != lo.rows * lo.rowLen)
+                    return false;
+                void* bp = nullptr;
+                std::size_t bb = 0;
+                if constexpr(!std::is_null_pointer_v<B>)
+                {
+                    bp = const_cast<void*>(static_cast<void const*>(alpaka::onHost::data(*buffer)));
+                    auto const ext = alpaka::onHost::getExtents(*buffer);
+                    bb = static_cast<std::size_t>(ext.product())
+                         * sizeof(alpaka::trait::GetValueType_t<std::decay_t<decltype(*buffer)>>);
+                    if(bb < a3b_scan_buffer_size(dt, li.rows * li.rowLen))
+                    {
+                        // a buffer sized for alpaka3's own multi-level scan may be smaller: use the cached scratch
+                        bp = nullptr;
+                        bb = 0;
+                    }
+                }
+                check(a3b_scan(streamOf(queue), dt, inclusive ? 1 : 0, li.ptr, const_cast<void*>(lo.ptr),
+                               li.rows * li.rowLen, nullptr, bp, bb),
+                      "alpaka3_b200 scan");
+                finish(queue);
+                ++routingStats().routed;
+                return true;
+            }
+        }
+
+        template<typename Q>
+        auto resolveExec(Q const& queue, auto exec)
+        {
+            if constexpr(std::is_same_v<std::decay_t<decltype(exec)>, alpaka::exec::AnyExecutor>)
+                return alpaka::onHost::defaultExecutor(queue.getDevice());
+            else
+                return exec;
+        }
+    } // namespace detail
+} // namespace alpaka3_b200
+
+namespace alpaka::onHost
+{
+    // ------------------------------------------------------------------------------------------ transformReduce
+    template<typename DataType, alpaka::concepts::DeviceKind T_DeviceKind, alpaka::concepts::QueueKind T_QueueKind>
+    inline void transformReduce(
+        Queue<Device<api::Cuda, T_DeviceKind>, T_QueueKind> const& queue,
+        alpaka::concepts::Executor auto const exec,
+        DataType const& neutralElement,
+        alpaka::concepts::IMdSpan auto out,
+        auto&& binaryReduceFn,
+        auto&& transformFn,
+        alpaka::concepts::IDataSource auto&&... in)
+        requires(std::same_as<DataType, alpaka::trait::GetValueType_t<ALPAKA_TYPEOF(out)>>)
+    {
+        if(alpaka3_b200::detail::tryTransformReduce<DataType>(queue, neutralElement, out, binaryReduceFn, transformFn, in...))
+            return;
+        ++alpaka3_b200::routingStats().forwarded;
+        internal::transformReduce(
+            queue,
+            alpaka3_b200::detail::resolveExec(queue, exec),
+            neutralElement,
+            out,
+            ALPAKA_FORWARD(binaryReduceFn),
+            ALPAKA_FORWARD(transformFn),
+            ALPAKA_FORWARD(in)...);
+    }
+
+    template<typename DataType, alpaka::concepts::DeviceKind T_DeviceKind, alpaka::concepts::QueueKind T_QueueKind>
+    inline void transformReduce(
+        Queue<Device<api::Cuda, T_DeviceKind>, T_QueueKind> const& queue,
+        DataType const& neutralElement,
+        alpaka::concepts::IMdSpan auto out,
+        auto&& binaryReduceFn,
+        auto&& transformFn,
+        alpaka::concepts::IDataSource auto&&... in)
+        requires(std::same_as<DataType, alpaka::trait::GetValueType_t<ALPAKA_TYPEOF(out)>>)
+    {
+        transformReduce(
+            queue,
+            defaultExecutor(queue.getDevice()),
+            neutralElement,
+            out,
+            ALPAKA_FORWARD(binaryReduceFn),
+            ALPAKA_FORWARD(transformFn),
+            ALPAKA_FORWARD(in)...);
+    }
+
+    // --------------------------------------------------------------------------------------------------- reduce
+    template<typename DataType, alpaka::concepts::DeviceKind T_DeviceKind, alpaka::concepts::QueueKind T_QueueKind>
+    inline void reduce(
+        Queue<Device<api::Cuda, T_DeviceKind>, T_QueueKind> const& queue,
+        alpaka::concepts::Executor auto const exec,
+        DataType const& neutralElement,
+        alpaka::concepts::IMdSpan auto out,
+        auto&& binaryReduceFn,
+        auto&& in) requires(std::same_as<DataType, alpaka::trait::GetValueType_t<ALPAKA_TYPEOF(out)>>)
+    {
+        if(alpaka3_b200::detail::tryTransformReduce<DataType>(queue, neutralElement, out, binaryReduceFn, std::identity{}, in))
+            return;
+        ++alpaka3_b200::routingStats().forwarded;
+        internal::transformReduce(
+            queue,
+            alpaka3_b200::detail::resolveExec(queue, exec),
+            neutralElement,
+            out,
+            ALPAKA_FORWARD(binaryReduceFn),
+            std::identity{},
+            ALPAKA_FORWARD(in));
+    }
+
+    template<typename DataType, alpaka::concepts::DeviceKind T_DeviceKind, alpaka::concepts::QueueKind T_QueueKind>
+    inline void reduce(
+        Queue<Device<api::Cuda, T_DeviceKind>, T_QueueKind> const& queue,
+        DataType const& neutralElement,
+        alpaka::concepts::IMdSpan auto out,
+        auto&& binaryReduceFn,
+        alpaka::concepts::IDataSource auto&& in)
+        requires(std::same_as<DataType, alpaka::trait::GetValueType_t<ALPAKA_TYPEOF(out)>>)
+    {
+        reduce(
+            queue,
+            defaultExecutor(queue.getDevice()),
+            neutralElement,
+            out,
+            ALPAKA_FORWARD(binaryReduceFn),
+            ALPAKA_FORWARD(in));
+    }
+
+    // ----------------------------------------------------------------------------------------------------- scans
+#define ALPAKA3_B200_SCAN_OVERLOADS(NAME, INCL, KIND)                                                                 \
+    template<alpaka::concepts::DeviceKind T_DeviceKind, alpaka::concepts::QueueKind T_QueueKind>                      \
+    void NAME(                                                                                                        \
+        Queue<Device<api::Cuda, T_DeviceKind>, T_QueueKind> const& queue,                                             \
+        alpaka::concepts::Executor auto exec,                                                                         \
+        alpaka::concepts::IMdSpan auto& buffer,                                                                       \
+        alpaka::concepts::IMdSpan auto& outputVec,                                                                    \
+        alpaka::concepts::IDataSource auto const& inputVec)                                                           \
+    {                                                                                                                 \
+        if(alpaka3_b200::detail::tryScan(queue, INCL, &buffer, outputVec, inputVec))                                  \
+            return;                                                                                                   \
+        ++alpaka3_b200::routingStats().forwarded;                                                                     \
+        auto devAcc = queue.getDevice();                                                                              \
+        auto ex = alpaka3_b200::detail::resolveExec(queue, exec);                                                     \
+        auto q = queue;                                                                                               \
+        internal::scan<internal::KIND>(q, devAcc, ex, buffer, outputVec, inputVec);                                   \
+    }                                                                                                                 \
+    template<alpaka::concepts::DeviceKind T_DeviceKind, alpaka::concepts::QueueKind T_QueueKind>                      \
+    void NAME(                                                                                                        \
+        Queue<Device<api::Cuda, T_DeviceKind>, T_QueueKind> const& queue,                                             \
+        alpaka::concepts::Executor auto exec,                                                                         \
+        alpaka::concepts::IMdSpan auto& outputVec,                                                                    \
+        alpaka::concepts::IDataSource auto const& inputVec)                                                           \
+    {                                                                                                                 \
+        if(alpaka3_b200::detail::tryScan(queue, INCL, nullptr, outputVec, inputVec))                                  \
+            return;                                                                                                   \
+        ++alpaka3_b200::routingStats().forwarded;                                                                     \
+        auto devAcc = queue.getDevice();                                                                              \
+        auto ex = alpaka3_b200::detail::resolveExec(queue, exec);                                                     \
+        auto q = queue;                                                                                               \
+        internal::scan<internal::KIND>(q, devAcc, ex, outputVec, inputVec);                                           \
+    }                                                                                                                 \
+    template<alpaka::concepts::DeviceKind T_DeviceKind, alpaka::concepts::QueueKind T_QueueKind>                      \
+    void NAME##InPlace(                                                                                               \
+        Queue<Device<api::Cuda, T_DeviceKind>, T_QueueKind> const& queue,                                             \
+        alpaka::concepts::Executor auto exec,                                                                         \
+        alpaka::concepts::IMdSpan auto& buffer,                                                                       \
+        alpaka::concepts::IMdSpan auto& dataVec)                                                                      \
+    {                                                                                                                 \
+        if(alpaka3_b200::detail::tryScan(queue, INCL, &buffer, dataVec, dataVec))                                     \
+            return;                                                                                                   \
+        ++alpaka3_b200::routingStats().forwarded;                                                                     \
+        auto devAcc = queue.getDevice();                                                                              \
+        auto ex = alpaka3_b200::detail::resolveExec(queue, exec);                                                     \
+        auto q = queue;                                                                                               \
+        internal::scan<internal::KIND>(q, devAcc, ex, buffer, dataVec, dataVec);                                      \
+    }                                                                                                                 \
+    template<alpaka::concepts::DeviceKind T_DeviceKind, alpaka::concepts::QueueKind T_QueueKind>                      \
+    void NAME##InPlace(                                                                                               \
+        Queue<Device<api::Cuda, T_DeviceKind>, T_QueueKind> const& queue,                                             \
+        alpaka::concepts::Executor auto exec,                                                                         \
+        alpaka::concepts::IMdSpan auto& dataVec)                                                                      \
+    {                                                                                                                 \
+        if(alpaka3_b200::detail::tryScan(queue, INCL, nullptr, dataVec, dataVec))                                     \
+            return;                                                                                                   \
+        ++alpaka3_b200::routingStats().forwarded;                                                                     \
+        auto devAcc = queue.getDevice();                                                                              \
+        auto ex = alpaka3_b200::detail::resolveExec(queue, exec);                                                     \
+        auto q = queue;                                                                                               \
+        internal::scan<internal::KIND>(q, devAcc, ex, dataVec, dataVec);                                              \
+    }
+
+    ALPAKA3_B200_SCAN_OVERLOADS(exclusiveScan, false, EXCLUSIVE_SCAN)
+    ALPAKA3_B200_SCAN_OVERLOADS(inclusiveScan, true, INCLUSIVE_SCAN)
+#undef ALPAKA3_B200_SCAN_OVERLOADS
+} // namespace alpaka::onHost

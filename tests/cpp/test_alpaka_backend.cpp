@@ -1,0 +1,224 @@
+/* alpaka3's own algorithm tests, re-expressed without Catch2, run through alpaka3's public onHost API on a CUDA queue
+ * with the alpaka3_b200 binding included: the covered calls go to libalpaka3_b200.so, the rest to alpaka3's own CUDA
+ * backend. Mirrors test/unit/algorithm/scan.cpp:74-197 (int iota, 4 sizes, exclusive/inclusive x out-of-place /
+ * in-place x with/without buffer, std::exclusive_scan / std::inclusive_scan as ground truth) and
+ * test/unit/algorithm/reduce.cpp:135-232 (int iota over N-D extents, plus / min / max, plus the generator source),
+ * plus BabelStream's dot (benchmark/babelstream/src/babelStreamMainTest.cpp:135-141, 337-345).
+ * Prints one line "PASS routed=<n> forwarded=<m>" and exits 0, or lists the failures and exits 1. */
+#include <alpaka3_b200/alpaka_backend.hpp>
+
+#include <cstdio>
+#include <cstdlib>
+#include <numeric>
+#include <vector>
+
+using namespace alpaka;
+
+namespace
+{
+    int failures = 0;
+
+    void expect(bool ok, char const* what, long long a = 0, long long b = 0)
+    {
+        if(!ok)
+        {
+            ++failures;
+            std::printf("FAIL %s (%lld vs %lld)\n", what, a, b);
+        }
+    }
+
+    struct MinValue
+    {
+        constexpr auto operator()(auto const& a, auto const& b) const
+        {
+            return math::min(a, b);
+        }
+    };
+
+    ALPAKA_FN_ACC void alpakaAtomicInvoke(MinValue const&, onAcc::concepts::Acc auto const& acc, auto* d, auto s)
+    {
+        onAcc::atomicMin(acc, d, s);
+    }
+
+    struct MaxValue
+    {
+        constexpr auto operator()(auto const& a, auto const& b) const
+        {
+            return math::max(a, b);
+        }
+    };
+
+    ALPAKA_FN_ACC void alpakaAtomicInvoke(MaxValue const&, onAcc::concepts::Acc auto const& acc, auto* d, auto s)
+    {
+        onAcc::atomicMax(acc, d, s);
+    }
+
+    struct DotMultiplication
+    {
+        constexpr auto operator()(concepts::Simd auto&& simdA, concepts::Simd auto&& simdB) const
+        {
+            return simdA * simdB;
+        }
+    };
+
+    struct Cube // not recognised: must be forwarded to alpaka3's own implementation
+    {
+        constexpr auto operator()(auto const& x) const
+        {
+            return x * x * x;
+        }
+    };
+
+    template<typename T>
+    void checkScan(auto& queue, auto& host, auto& dev, std::size_t n, bool inclusive, char const* what)
+    {
+        auto back = onHost::allocHost<T>(Vec{n});
+        onHost::memcpy(queue, back, dev);
+        onHost::wait(queue);
+        std::vector<T> want(n);
+        if(inclusive)
+            std::inclusive_scan(host.data(), host.data() + n, want.data());
+        else
+            std::exclusive_scan(host.data(), host.data() + n, want.data(), T{0});
+        std::size_t bad = 0;
+        for(std::size_t i = 0; i < n; ++i)
+            bad += back.data()[i] != want[i];
+        expect(bad == 0, what, static_cast<long long>(bad), static_cast<long long>(n));
+    }
+
+    void scanTests(auto& dev, auto& queue, auto exec)
+    {
+        using T = int;
+        for(std::size_t n : {std::size_t{12}, std::size_t{1024}, std::size_t{654321}, std::size_t{20971520}})
+        {
+            auto ext = Vec{n};
+            auto in = onHost::alloc<T>(dev, ext);
+            auto out = onHost::alloc<T>(dev, ext);
+            auto host = onHost::allocHostLike(in);
+            T c = 0;
+            for(auto& v : host)
+                v = c++;
+            auto buffer = onHost::alloc<std::byte>(dev, onHost::getScanBufferSize<T>(in.getExtents()));
+            for(int incl = 0; incl < 2; ++incl)
+            {
+                onHost::memcpy(queue, in, host);
+                if(incl)
+                    onHost::inclusiveScan(queue, exec, out, in);
+                else
+                    onHost::exclusiveScan(queue, exec, out, in);
+                checkScan<T>(queue, host, out, n, incl, "scan, no buffer");
+                if(incl)
+                    onHost::inclusiveScanInPlace(queue, exec, in);
+                else
+                    onHost::exclusiveScanInPlace(queue, exec, in);
+                checkScan<T>(queue, host, in, n, incl, "scan, no buffer, in-place");
+                onHost::memcpy(queue, in, host);
+                if(incl)
+                    onHost::inclusiveScan(queue, exec, buffer, out, in);
+                else
+                    onHost::exclusiveScan(queue, exec, buffer, out, in);
+                checkScan<T>(queue, host, out, n, incl, "scan, with buffer");
+                if(incl)
+                    onHost::inclusiveScanInPlace(queue, exec, buffer, in);
+                else
+                    onHost::exclusiveScanInPlace(queue, exec, buffer, in);
+                checkScan<T>(queue, host, in, n, incl, "scan, with buffer, in-place");
+            }
+        }
+    }
+
+    template<typename T>
+    T hostReduce(int op, std::size_t n, T init)
+    {
+        T r = init;
+        for(std::size_t i = 0; i < n; ++i)
+        {
+            T const v = static_cast<T>(i);
+            r = op == 0 ? static_cast<T>(static_cast<unsigned>(r) + static_cast<unsigned>(v)) : (op == 1 ? std::min(r, v) : std::max(r, v));
+        }
+        return r;
+    }
+
+    void reduceOne(auto& dev, auto& queue, auto exec, auto extents)
+    {
+        using T = int;
+        auto in = onHost::alloc<T>(dev, extents);
+        auto host = onHost::allocHostLike(in);
+        T c = 0;
+        for(auto& v : host)
+            v = c++;
+        onHost::memcpy(queue, in, host);
+        auto out = onHost::alloc<T>(dev, extents.fill(1));
+        auto outHost = onHost::allocHostLike(out);
+        std::size_t const n = static_cast<std::size_t>(extents.product());
+        for(int op = 0; op < 3; ++op)
+        {
+            if(op == 0)
+                onHost::reduce(queue, exec, T{0}, out, std::plus{}, in);
+            else if(op == 1)
+                onHost::reduce(queue, exec, std::numeric_limits<T>::max(), out, ScalarFunc{MinValue{}}, in);
+            else
+                onHost::reduce(queue, exec, std::numeric_limits<T>::min(), out, ScalarFunc{MaxValue{}}, in);
+            onHost::memcpy(queue, outHost, out);
+            onHost::wait(queue);
+            T const want = hostReduce<T>(op, n, op == 0 ? 0 : (op == 1 ? std::numeric_limits<T>::max() : std::numeric_limits<T>::min()));
+            expect(*outHost.data() == want, "reduce", *outHost.data(), want);
+        }
+        // generator source (not device memory): forwarded to alpaka3's own implementation
+        auto generator = LinearizedIdxGenerator{extents};
+        onHost::reduce(queue, exec, T{0}, out, std::plus{}, generator);
+        onHost::memcpy(queue, outHost, out);
+        onHost::wait(queue);
+        expect(*outHost.data() == hostReduce<T>(0, n, 0), "reduce generator", *outHost.data(), hostReduce<T>(0, n, 0));
+    }
+
+    void transformReduceTests(auto& dev, auto& queue, auto exec)
+    {
+        // BabelStream dot: a = 0.1, b = 0.2 over 2^20 doubles -> N * a * b
+        std::size_t const n = std::size_t{1} << 20;
+        auto a = onHost::alloc<double>(dev, Vec{n});
+        auto b = onHost::allocLike(dev, a);
+        onHost::fill(queue, a, 0.1);
+        onHost::fill(queue, b, 0.2);
+        auto out = onHost::alloc<double>(dev, Vec{std::size_t{1}});
+        auto outHost = onHost::allocHostLike(out);
+        onHost::transformReduce(queue, exec, 0.0, out, std::plus{}, DotMultiplication{}, a, b);
+        onHost::memcpy(queue, outHost, out);
+        onHost::wait(queue);
+        double const want = static_cast<double>(n) * 0.1 * 0.2;
+        expect(std::abs(*outHost.data() - want) <= 1e-12 * want, "dot", static_cast<long long>(*outHost.data()), static_cast<long long>(want));
+        // a transform the binding does not recognise: alpaka3's own kernel computes it
+        onHost::transformReduce(queue, exec, 0.0, out, std::plus{}, Cube{}, a);
+        onHost::memcpy(queue, outHost, out);
+        onHost::wait(queue);
+        double const want2 = static_cast<double>(n) * (0.1 * 0.1 * 0.1);
+        expect(std::abs(*outHost.data() - want2) <= 1e-9 * want2, "transformReduce forwarded", 0, 0);
+    }
+} // namespace
+
+int main()
+{
+    auto selector = onHost::makeDeviceSelector(onHost::DeviceSpec{api::cuda, deviceKind::nvidiaGpu});
+    if(!selector.isAvailable())
+    {
+        std::printf("SKIP no CUDA device\n");
+        return 77;
+    }
+    auto dev = selector.makeDevice(0);
+    auto queue = dev.makeQueue();
+    auto exec = exec::gpuCuda;
+    scanTests(dev, queue, exec);
+    // extents of test/unit/algorithm/reduce.cpp:150-151
+    reduceOne(dev, queue, exec, Vec{5, 7, 3, 11});
+    reduceOne(dev, queue, exec, Vec{93, 7, 123});
+    reduceOne(dev, queue, exec, Vec{5, 7, 4111});
+    reduceOne(dev, queue, exec, Vec{5, 7, 3});
+    reduceOne(dev, queue, exec, Vec{7, 3});
+    reduceOne(dev, queue, exec, Vec{3});
+    transformReduceTests(dev, queue, exec);
+    auto& st = alpaka3_b200::routingStats();
+    if(failures == 0)
+        std::printf("PASS routed=%llu forwarded=%llu\n", static_cast<unsigned long long>(st.routed.load()),
+                    static_cast<unsigned long long>(st.forwarded.load()));
+    return failures == 0 ? 0 : 1;
+}
