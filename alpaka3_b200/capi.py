@@ -55,6 +55,11 @@ SIGNATURES = {
     "a3b_transform_reduce_partial": [_P, _I, _I, _I, _P, _P, _U64, _P, _P],
     "a3b_transform_reduce_noalloc": [_P, _I, _I, _I, _P, _P, _U64, _P, _P],
     "a3b_reduce_2d": [_P, _I, _I, _P, _U64, _U64, _U64, _P, _P],
+    "a3b_ipc_handle_size": [],
+    "a3b_peer_group_create": [_I, _I, _P, _P],
+    "a3b_peer_group_connect": [_P, _P],
+    "a3b_peer_group_destroy": [_P],
+    "a3b_transform_reduce_allranks": [_P, _P, _I, _I, _I, _P, _P, _U64, _P, _P],
     "a3b_scan_buffer_size": [_I, _U64],
     "a3b_scan": [_P, _I, _I, _P, _P, _U64, _P, _P, ctypes.c_size_t],
     "a3b_scan_debug_stall": [_P, _I, _P, _P, _U64, _U64],
@@ -63,7 +68,8 @@ SIGNATURES = {
     "a3b_heat_step": [_P, _P, _P, _U64, _U64, _U64, _U64, _U64, _D, _D],
     "a3b_heat_init": [_P, _P, _U64, _U64, _U64, _U64, _U64, _D, _D],
 }
-_RESTYPES = {"a3b_last_error": ctypes.c_char_p, "a3b_scan_buffer_size": ctypes.c_size_t}
+_RESTYPES = {"a3b_last_error": ctypes.c_char_p, "a3b_scan_buffer_size": ctypes.c_size_t,
+             "a3b_ipc_handle_size": ctypes.c_size_t}
 
 
 class LibraryNotBuilt(RuntimeError):

@@ -100,6 +100,30 @@ namespace a3b
         return (reinterpret_cast<uintptr_t>(p) & 15u) == 0u;
     }
 
+    // ------------------------------------------------------------------------------------------ peer groups
+    // One slot buffer per rank, mapped into every other rank's address space (CUDA IPC over NVLink). Slot
+    // [parity][r] holds rank r's 8-byte value and the epoch of the call that wrote it; the parity of the epoch
+    // double-buffers consecutive calls (a rank can be at most one call ahead of another).
+    constexpr int kMaxPeers = 8;
+    constexpr size_t kPeerSlotBytes = 4096;
+
+    struct PeerSlots
+    {
+        unsigned long long* slots[kMaxPeers]; // rank r's slot buffer, as addressed from this device
+        int world;
+        int rank;
+        unsigned epoch;
+    };
+
+} // namespace a3b
+
+struct a3b_peer_group;
+
+namespace a3b
+{
+    // Slot pointers of a connected group for the current device; advances the group's call epoch.
+    int peerSlots(a3b_peer_group* g, PeerSlots* out);
+
     // ------------------------------------------------------------------------------------------ device side
     constexpr unsigned kErrTimeout = 1u;
 

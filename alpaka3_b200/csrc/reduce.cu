@@ -212,24 +212,19 @@ namespace a3b
             }
         }
 
-        // PITCHED: rows of rowLen elements, rowPitch bytes apart; packs never straddle rows (rowLen % W == 0).
+        // This block's partial (identical in every thread on return). PITCHED: rows of rowLen elements, rowPitch bytes
+        // apart; packs never straddle rows (rowLen % W == 0).
         template<typename T, int W, int ROp, int XOp, bool PITCHED>
-        __global__ void __launch_bounds__(kBlock) reduceKernel(
+        __device__ __forceinline__ typename AccOf<T, ROp>::type blockPartial(
             T const* __restrict__ in0,
             T const* __restrict__ in1,
             uint64_t n,
             uint64_t rowLen,
             uint64_t rowPitch,
             T neutral,
-            void* out,
-            bool rawPartial,
-            ReduceScratch* scratch,
-            typename AccOf<T, ROp>::type* partials)
+            typename AccOf<T, ROp>::type* smem)
         {
             using A = typename AccOf<T, ROp>::type;
-            __shared__ A smem[kWarps];
-            __shared__ bool amLast;
-
             A const neutralA = widen<A>(neutral);
             A acc[kUnroll];
 #pragma unroll
@@ -299,6 +294,27 @@ namespace a3b
             for(int u = 1; u < kUnroll; ++u)
                 v = combine<A, ROp>(v, acc[u]);
             v = blockReduce<A, ROp>(v, smem);
+            return v;
+        }
+
+        template<typename T, int W, int ROp, int XOp, bool PITCHED>
+        __global__ void __launch_bounds__(kBlock) reduceKernel(
+            T const* __restrict__ in0,
+            T const* __restrict__ in1,
+            uint64_t n,
+            uint64_t rowLen,
+            uint64_t rowPitch,
+            T neutral,
+            void* out,
+            bool rawPartial,
+            ReduceScratch* scratch,
+            typename AccOf<T, ROp>::type* partials)
+        {
+            using A = typename AccOf<T, ROp>::type;
+            __shared__ A smem[kWarps];
+            __shared__ bool amLast;
+            A const neutralA = widen<A>(neutral);
+            A const v = blockPartial<T, W, ROp, XOp, PITCHED>(in0, in1, n, rowLen, rowPitch, neutral, smem);
 
             if(threadIdx.x == 0)
             {
@@ -320,6 +336,198 @@ namespace a3b
             {
                 writeResult<T, A>(out, r, rawPartial);
                 scratch->ticket = 0u; // ready for the next call on this stream
+            }
+        }
+
+        // ---------------------------------------------------------------- fused with the all-reduce over peers
+        __device__ __forceinline__ void stRelaxedSys(unsigned long long* p, unsigned long long v)
+        {
+            asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+        }
+
+        __device__ __forceinline__ void stReleaseSys(unsigned long long* p, unsigned long long v)
+        {
+            asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+        }
+
+        __device__ __forceinline__ unsigned long long ldAcquireSys(unsigned long long const* p)
+        {
+            unsigned long long v;
+            asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+            return v;
+        }
+
+        __device__ __forceinline__ unsigned long long ldRelaxedSys(unsigned long long const* p)
+        {
+            unsigned long long v;
+            asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+            return v;
+        }
+
+        // Local reduction as reduceKernel; the last block then stores the unrounded local total into slot
+        // [epoch parity][rank] of every rank's slot buffer (value, then the epoch with release semantics), waits for
+        // the world's values in its own buffer and combines them in rank order: every rank computes the same bits.
+        template<typename T, int W, int ROp, int XOp>
+        __global__ void __launch_bounds__(kBlock) reduceAllRanksKernel(
+            T const* __restrict__ in0,
+            T const* __restrict__ in1,
+            uint64_t n,
+            T neutral,
+            void* out,
+            ReduceScratch* scratch,
+            typename AccOf<T, ROp>::type* partials,
+            PeerSlots peers,
+            unsigned* errWord,
+            uint64_t timeoutNs)
+        {
+            using A = typename AccOf<T, ROp>::type;
+            __shared__ A smem[kWarps];
+            __shared__ bool amLast;
+            A const neutralA = widen<A>(neutral);
+            A const v = blockPartial<T, W, ROp, XOp, false>(in0, in1, n, n, 0, neutral, smem);
+            if(threadIdx.x == 0)
+            {
+                partials[blockIdx.x] = v;
+                __threadfence();
+                unsigned const t = atomicAdd(&scratch->ticket, 1u);
+                amLast = (t == gridDim.x - 1u);
+            }
+            __syncthreads();
+            if(!amLast)
+                return;
+            __threadfence();
+            A r = neutralA;
+            for(unsigned b = threadIdx.x; b < gridDim.x; b += kBlock)
+                r = combine<A, ROp>(r, __ldcg(partials + b));
+            r = blockReduce<A, ROp>(r, smem);
+            if(threadIdx.x != 0)
+                return;
+            scratch->ticket = 0u;
+            static_assert(sizeof(A) <= 8, "partials are exchanged as 8-byte words");
+            unsigned long long bits = 0;
+            memcpy(&bits, &r, sizeof(A));
+            unsigned const par = peers.epoch & 1u;
+            for(int q = 0; q < peers.world; ++q)
+            {
+                unsigned long long* slot = peers.slots[q] + 2 * (par * kMaxPeers + peers.rank);
+                stRelaxedSys(slot, bits);
+                stReleaseSys(slot + 1, peers.epoch);
+            }
+            A total = neutralA;
+            bool ok = true;
+            uint64_t const t0 = globalTimerNs();
+            for(int q = 0; q < peers.world && ok; ++q)
+            {
+                unsigned long long const* slot = peers.slots[peers.rank] + 2 * (par * kMaxPeers + q);
+                while(ldAcquireSys(slot + 1) != peers.epoch)
+                {
+                    if(globalTimerNs() - t0 > timeoutNs)
+                    {
+                        ok = false;
+                        break;
+                    }
+                    __nanosleep(32);
+                }
+                if(ok)
+                {
+                    unsigned long long const vb = ldRelaxedSys(slot);
+                    A val;
+                    memcpy(&val, &vb, sizeof(A));
+                    total = combine<A, ROp>(total, val);
+                }
+            }
+            if(!ok)
+                atomicOr(errWord, kErrTimeout);
+            writeResult<T, A>(out, total, false);
+        }
+
+        template<typename T, int W, int ROp, int XOp>
+        int launchAllRanks(cudaStream_t s, a3b_peer_group* g, T const* in0, T const* in1, uint64_t n, T neutral, void* out)
+        {
+            using A = typename AccOf<T, ROp>::type;
+            DeviceProps const* props = nullptr;
+            int rc = currentDevice(&props);
+            if(rc)
+                return rc;
+            static int resident[64] = {0};
+            int& r = resident[props->ordinal];
+            if(r == 0)
+            {
+                int b = 0;
+                A3B_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b, reduceAllRanksKernel<T, W, ROp, XOp>, kBlock, 0));
+                r = b > 0 ? b : 1;
+            }
+            uint64_t const packs = n / W + 1;
+            uint64_t const want = (packs + static_cast<uint64_t>(kBlock) * kUnroll - 1) / (kBlock * kUnroll);
+            uint64_t const full = static_cast<uint64_t>(props->smCount) * r;
+            int const grid = static_cast<int>(want < full ? (want > 0 ? want : 1) : full);
+            void* scr = nullptr;
+            rc = streamScratch(s, kScratchReduce, sizeof(ReduceScratch) + sizeof(A) * static_cast<size_t>(full), &scr);
+            if(rc)
+                return rc;
+            PeerSlots peers;
+            rc = peerSlots(g, &peers);
+            if(rc)
+                return rc;
+            auto* hdr = static_cast<ReduceScratch*>(scr);
+            reduceAllRanksKernel<T, W, ROp, XOp><<<grid, kBlock, 0, s>>>(
+                in0, in1, n, neutral, out, hdr, reinterpret_cast<A*>(hdr + 1), peers, props->errWord, waitTimeoutNs());
+            A3B_CHECK_LAUNCH("transform_reduce_allranks launch");
+            return A3B_OK;
+        }
+
+        template<typename T, int ROp, int XOp>
+        int allRanksLayout(cudaStream_t s, a3b_peer_group* g, T const* in0, T const* in1, uint64_t n, T neutral, void* out)
+        {
+            auto al = [&](uintptr_t a)
+            {
+                auto ok = [&](void const* p) { return (reinterpret_cast<uintptr_t>(p) & (a - 1u)) == 0u; };
+                return ok(in0) && (XOp != A3B_XFORM_PRODUCT || ok(in1));
+            };
+            constexpr int W = 16 / sizeof(T);
+            if(al(32))
+                return launchAllRanks<T, 2 * W, ROp, XOp>(s, g, in0, in1, n, neutral, out);
+            if(al(16))
+                return launchAllRanks<T, W, ROp, XOp>(s, g, in0, in1, n, neutral, out);
+            return launchAllRanks<T, 1, ROp, XOp>(s, g, in0, in1, n, neutral, out);
+        }
+
+        template<typename T, int ROp>
+        int allRanksXform(cudaStream_t s, a3b_peer_group* g, int xop, T const* in0, T const* in1, uint64_t n, T neutral, void* out)
+        {
+            switch(xop)
+            {
+            case A3B_XFORM_IDENTITY:
+                return allRanksLayout<T, ROp, A3B_XFORM_IDENTITY>(s, g, in0, in1, n, neutral, out);
+            case A3B_XFORM_SQUARE:
+                return allRanksLayout<T, ROp, A3B_XFORM_SQUARE>(s, g, in0, in1, n, neutral, out);
+            case A3B_XFORM_PRODUCT:
+                A3B_REQUIRE(in1, "product transform needs two inputs");
+                return allRanksLayout<T, ROp, A3B_XFORM_PRODUCT>(s, g, in0, in1, n, neutral, out);
+            default:
+                setError("unknown transform op %d", xop);
+                return A3B_ERR_INVALID;
+            }
+        }
+
+        template<typename T>
+        int allRanksReduce(cudaStream_t s, a3b_peer_group* g, int rop, int xop, void const* in0, void const* in1, uint64_t n,
+                           void const* neutral, void* out)
+        {
+            T const nv = *static_cast<T const*>(neutral);
+            auto i0 = static_cast<T const*>(in0);
+            auto i1 = static_cast<T const*>(in1);
+            switch(rop)
+            {
+            case A3B_REDUCE_PLUS:
+                return allRanksXform<T, A3B_REDUCE_PLUS>(s, g, xop, i0, i1, n, nv, out);
+            case A3B_REDUCE_MIN:
+                return allRanksXform<T, A3B_REDUCE_MIN>(s, g, xop, i0, i1, n, nv, out);
+            case A3B_REDUCE_MAX:
+                return allRanksXform<T, A3B_REDUCE_MAX>(s, g, xop, i0, i1, n, nv, out);
+            default:
+                setError("unknown reduce op %d", rop);
+                return A3B_ERR_INVALID;
             }
         }
 
@@ -676,6 +884,33 @@ extern "C"
             return noAllocReduce<float>(s, reduce_op, transform_op, in0, in1, n, neutral, out);
         case A3B_F64:
             return noAllocReduce<double>(s, reduce_op, transform_op, in0, in1, n, neutral, out);
+        default:
+            setError("unknown dtype %d", dtype);
+            return A3B_ERR_INVALID;
+        }
+    }
+
+    int a3b_transform_reduce_allranks(a3b_stream_t stream, a3b_peer_group* group, int dtype, int reduce_op,
+                                      int transform_op, void const* in0, void const* in1, uint64_t n,
+                                      void const* neutral, void* out)
+    {
+        A3B_REQUIRE(group && out && neutral, "null group/out/neutral");
+        A3B_REQUIRE(in0 || n == 0, "null input");
+        auto s = static_cast<cudaStream_t>(stream);
+        switch(dtype)
+        {
+        case A3B_I32:
+            return allRanksReduce<int32_t>(s, group, reduce_op, transform_op, in0, in1, n, neutral, out);
+        case A3B_U32:
+            return allRanksReduce<uint32_t>(s, group, reduce_op, transform_op, in0, in1, n, neutral, out);
+        case A3B_I64:
+            return allRanksReduce<int64_t>(s, group, reduce_op, transform_op, in0, in1, n, neutral, out);
+        case A3B_U64:
+            return allRanksReduce<uint64_t>(s, group, reduce_op, transform_op, in0, in1, n, neutral, out);
+        case A3B_F32:
+            return allRanksReduce<float>(s, group, reduce_op, transform_op, in0, in1, n, neutral, out);
+        case A3B_F64:
+            return allRanksReduce<double>(s, group, reduce_op, transform_op, in0, in1, n, neutral, out);
         default:
             setError("unknown dtype %d", dtype);
             return A3B_ERR_INVALID;

@@ -221,3 +221,51 @@ class HeatSlab:
         for r in self.pending:
             r.wait()
         self.pending = []
+
+
+class PeerGroup:
+    """The ranks of this node connected through mapped slot buffers (a3b_peer_group): the fused reduce + all-reduce
+    stores each rank's partial straight into every peer's memory over NVLink from inside the reduction kernel."""
+
+    def __init__(self):
+        import ctypes
+        from . import capi
+        self.world, self.rank = _world()
+        L = capi.lib()
+        hsz = L.a3b_ipc_handle_size()
+        handle = (ctypes.c_char * hsz)()
+        self.g = ctypes.c_void_p()
+        capi.call("a3b_peer_group_create", self.world, self.rank, ctypes.byref(self.g), handle)
+        mine = bytes(handle)
+        if self.world > 1:
+            handles = [None] * self.world
+            dist.all_gather_object(handles, mine)
+        else:
+            handles = [mine]
+        blob = b"".join(handles)
+        arr = (ctypes.c_char * len(blob)).from_buffer_copy(blob)
+        capi.call("a3b_peer_group_connect", self.g, arr)
+        if self.world > 1:
+            dist.barrier()
+
+    def close(self):
+        from . import capi
+        if self.g:
+            capi.call("a3b_peer_group_destroy", self.g)
+            self.g = None
+
+    def transform_reduce(self, neutral, reduce_fn, transform_fn, in0_local, in1_local=None, out=None):
+        """Sharded onHost::transformReduce in one launch per rank (fused with the all-reduce); every rank gets the
+        same bits. All ranks must make the same sequence of calls."""
+        import ctypes
+        from . import algo, capi
+        code = algo.dtype_code(in0_local)
+        if out is None:
+            out = torch.empty(1, dtype=in0_local.dtype, device=in0_local.device)
+        if neutral is None:
+            neutral = algo._neutral(reduce_fn, code)
+        keep, p = algo._host_scalar(neutral, code)
+        capi.call("a3b_transform_reduce_allranks", algo.stream_handle(), self.g, code, algo.REDUCE[reduce_fn],
+                  algo.XFORM[transform_fn], algo._ptr(in0_local), algo._ptr(in1_local), in0_local.numel(), p,
+                  algo._ptr(out))
+        return out

@@ -4,8 +4,10 @@
     torchrun --nproc-per-node N bench.py --gpus N ...      (one rank per GPU, NCCL)
 
 A step is one pass of the hot path over the workload: every rank reduces its contiguous shard of the 2^30 seeded
-fp32 values (one kernel launch through the C ABI), and for N > 1 the 8-byte partials are combined by an NCCL
-all-reduce. `value` is the whole-job throughput (4 * 2^30 bytes per step / max-over-ranks step time) with the inputs
+fp32 values in one kernel launch through the C ABI; for N > 1 that same kernel stores its unrounded partial into every
+peer's mapped slot buffer over NVLink and combines the world's partials in rank order (a3b_transform_reduce_allranks;
+`--collective nccl` uses an NCCL all-reduce after the kernel instead, and the fused run also reports that variant's
+time). `value` is the whole-job throughput (4 * 2^30 bytes per step / max-over-ranks step time) with the inputs
 resident in HBM; `e2e` is the same step through the C ABI from pinned HOST memory (host->device copy of each rank's
 shard and device->host read of the result inside the timed region). At N = 1 the line also carries `parts`: the other
 kernels the metric names (BabelStream triad and dot at 2^25 fp64, exclusive scan of 2^30 int32, inclusive scan of
@@ -29,7 +31,7 @@ METRIC = "triad/dot/reduce/scan HBM GB/s (fraction of ~8 TB/s) at 1/2/4/8 B200"
 N_SUMSQ = 1 << 30
 SEED = 0x5EED0001
 WORKLOAD = ("transformReduce sum of squares (std::plus, x*x) over 2^30 fp32 uniform[-1,1) from a seeded Philox "
-            "stream, contiguous shards per rank, NCCL all-reduce of the fp64 partials")
+            "stream, contiguous shards per rank, fp64 partials combined across ranks")
 
 
 def peaks():
@@ -159,42 +161,58 @@ def run_b200(args):
     s = torch.cuda.current_stream()
     launches = [0]
 
+    group = adist.PeerGroup() if dist_on and args.collective == "fused" else None
+
     def step(ev):
         if ev:
             ev[0].record(s)
-        if dist_on:
+        if group is not None:
+            group.transform_reduce(0.0, "plus", "square", x, out=out)  # one launch: reduce + all-reduce
+        elif dist_on:
             algo.transform_reduce_partial("plus", "square", x, partial=partial)
         else:
             algo.transform_reduce(0.0, out, "plus", "square", x)
         if ev:
             ev[1].record(s)
             launches[0] += 1
-        if dist_on:
+        if dist_on and group is None:
             adist.allreduce_partial(partial, "plus")
+
+    def nccl_step(ev):
+        algo.transform_reduce_partial("plus", "square", x, partial=partial)
+        adist.allreduce_partial(partial, "plus")
 
     sampler = ClockSampler(pci_bus_id(torch, local))
     sampler.start()
     ms, kern_ms = time_steps(torch, dist_on, step, args.steps, args.warmup)
     sampler.stop()
     ms = max_over_ranks(torch, dist_on, ms)
+    nccl_ms = None
+    if group is not None:
+        nccl_ms, _ = time_steps(torch, dist_on, nccl_step, args.steps, args.warmup, kernel_events=False)
+        nccl_ms = max_over_ranks(torch, dist_on, nccl_ms)
     total_bytes = 4.0 * N_SUMSQ
     value = total_bytes / (ms * 1e-3) / 1e9
     kern_gbs = 4.0 * n_local / (kern_ms * 1e-3) / 1e9
-    result = float(partial.item()) if dist_on else float(out.item())
+    result = float(out.item()) if (group is not None or not dist_on) else float(partial.item())
 
     # ---------------------------------------------------------------- e2e: host buffers through the C ABI
     e2e = None
     if not args.no_e2e:
         host = torch.empty(n_local, dtype=torch.float32, pin_memory=True)
         host.copy_(x.cpu())
-        res_host = torch.empty(1, dtype=torch.float64 if dist_on else torch.float32, pin_memory=True)
+        res_host = torch.empty(1, dtype=torch.float64 if (dist_on and group is None) else torch.float32,
+                               pin_memory=True)
         sh = algo.stream_handle()
         import ctypes
 
         def e2e_step(ev):
             capi.call("a3b_memcpy_async", ctypes.c_void_p(x.data_ptr()), ctypes.c_void_p(host.data_ptr()),
                       4 * n_local, sh)
-            if dist_on:
+            if group is not None:
+                group.transform_reduce(0.0, "plus", "square", x, out=out)
+                src = out
+            elif dist_on:
                 algo.transform_reduce_partial("plus", "square", x, partial=partial)
                 adist.allreduce_partial(partial, "plus")
                 src = partial
@@ -208,7 +226,7 @@ def run_b200(args):
         e_ms, _ = time_steps(torch, dist_on, e2e_step, e_steps, 1, kernel_events=False)
         e_ms = max_over_ranks(torch, dist_on, e_ms)
         e2e = {"value": total_bytes / (e_ms * 1e-3) / 1e9, "unit": "GB/s", "h2d_bytes_per_step": 4 * N_SUMSQ,
-               "d2h_bytes_per_step": (8 if dist_on else 4) * world, "steps": e_steps,
+               "d2h_bytes_per_step": res_host.element_size() * world, "steps": e_steps,
                "path": "a3b_memcpy_async(H2D, pinned) + a3b_transform_reduce + a3b_memcpy_async(D2H)"}
         del host
 
@@ -229,7 +247,8 @@ def run_b200(args):
             "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded Philox4x32-10, uniform [-1,1))",
             "config": {"workload": WORKLOAD, "n": N_SUMSQ, "bytes_per_step": int(total_bytes),
                        "per_rank_elements": n_local, "l2": "inputs larger than L2 (4.29 GB total, >= 537 MB per GPU)",
-                       "parallelism": f"shard{world}+allreduce" if dist_on else "single GPU"},
+                       "parallelism": (f"shard{world}+fused peer all-reduce" if group is not None else
+                                       f"shard{world}+NCCL all-reduce") if dist_on else "single GPU"},
             "result": result,
             "roofline": {"bound": "hbm", "achieved": round(kern_gbs, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(kern_gbs / peak, 4), "peak_kind": peak_kind,
@@ -238,6 +257,8 @@ def run_b200(args):
                          "kernel_ms": round(kern_ms, 5)},
             "e2e": e2e, "gpu_launches": launches[0], "clocks": sampler.summary(),
         }
+        if nccl_ms is not None:
+            line["nccl_allreduce_ms_per_step"] = round(nccl_ms, 5)
         if cpu:
             line["cpu_baseline"] = cpu
         if parts:
@@ -245,6 +266,10 @@ def run_b200(args):
         print(json.dumps(line), flush=True)
     if dist_on:
         import torch.distributed as dist
+        torch.cuda.synchronize()
+        dist.barrier()
+        if group is not None:
+            group.close()
         dist.barrier()
         dist.destroy_process_group()
 
@@ -356,7 +381,7 @@ def run_reference(args):
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 3), "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic (seeded Philox4x32-10, uniform [-1,1))",
-        "config": {"workload": WORKLOAD.replace(", contiguous shards per rank, NCCL all-reduce of the fp64 partials",
+        "config": {"workload": WORKLOAD.replace(", contiguous shards per rank, fp64 partials combined across ranks",
                                                 "") + ", whole input on the host", "n": N_SUMSQ,
                    "bytes_per_step": 4 * N_SUMSQ, "parallelism": "host OpenMP"},
         "result": float(r),
@@ -431,6 +456,9 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=8.0)
+    ap.add_argument("--collective", default="fused", choices=["fused", "nccl"],
+                    help="N > 1: combine the per-rank partials inside the reduction kernel over mapped peer memory "
+                         "(fused) or with an NCCL all-reduce after it")
     ap.add_argument("--profile-case", default=None,
                     choices=["sumsq", "triad", "copy", "dot", "scan_i32", "scan_u64", "nbody", "heat"],
                     help="run only this kernel (for ncu captures of a small case); prints a short line")

@@ -184,6 +184,28 @@ A3B_API int a3b_transform_reduce_noalloc(a3b_stream_t stream, int dtype, int red
 A3B_API int a3b_reduce_2d(a3b_stream_t stream, int dtype, int reduce_op, void const* in, uint64_t rows, uint64_t row_len,
                   uint64_t row_pitch_bytes, void const* neutral, void* out);
 
+/* --------------------------------------------------------------------------------------- multi-GPU (one node) */
+
+/* A peer group connects the ranks of one node (one process per GPU) through a small slot buffer per rank that every
+ * other rank maps over NVLink (CUDA IPC). Protocol: each rank calls a3b_peer_group_create on its device, exchanges
+ * the a3b_ipc_handle_size() bytes written to `local_handle` with all ranks (any host channel), then calls
+ * a3b_peer_group_connect with the world handles in rank order. No counterpart in alpaka3, which has no multi-device
+ * layer. */
+typedef struct a3b_peer_group a3b_peer_group;
+A3B_API size_t a3b_ipc_handle_size(void);
+A3B_API int a3b_peer_group_create(int world, int rank, a3b_peer_group** group, void* local_handle);
+A3B_API int a3b_peer_group_connect(a3b_peer_group* group, void const* handles);
+A3B_API int a3b_peer_group_destroy(a3b_peer_group* group);
+
+/* onHost::transformReduce over data sharded across the ranks of a peer group, fused with the all-reduce: one launch
+ * per rank reduces the local shard, its last block stores the unrounded partial into every rank's slot (peer stores
+ * over NVLink), waits (bounded) for all ranks' partials and combines them in rank order, so every rank writes the
+ * same bits to its `out`. All ranks must make the same sequence of calls. A wait that runs out sets bit 0 of the
+ * device error word (a3b_get_device_error). */
+A3B_API int a3b_transform_reduce_allranks(a3b_stream_t stream, a3b_peer_group* group, int dtype, int reduce_op,
+                                          int transform_op, void const* in0, void const* in1, uint64_t n,
+                                          void const* neutral, void* out);
+
 /* ------------------------------------------------------------------------------------------------------ scan */
 
 /* onHost::getScanBufferSize<T>(extents) (include/alpaka/onHost/algo/scan.hpp:26-30): bytes of the caller buffer that

@@ -28,6 +28,21 @@ def main():
     exact = port.sumsq(port.gen_f32(n, -1.0, 1.0))
     res["sumsq_rel"] = abs(got - exact) / exact
 
+    # the same reduction fused with the all-reduce over mapped peer slots
+    group = ad.PeerGroup()
+    fused = group.transform_reduce(0.0, "plus", "square", x).item()
+    res["sumsq_fused_rel"] = abs(fused - exact) / exact
+    res["fused_matches_nccl"] = abs(fused - got) <= 1e-6 * abs(got)
+    for _ in range(5):  # consecutive calls reuse the slots through the epoch parity
+        again = group.transform_reduce(0.0, "plus", "square", x).item()
+    res["fused_repeat_ok"] = again == fused
+    xi0 = torch.randint(-1000, 1000, (e - b,), dtype=torch.int32, device=dev)
+    mx = [torch.zeros(1, dtype=torch.int32, device=dev) for _ in range(world)]
+    torch.distributed.all_gather(mx, xi0.max().reshape(1))
+    res["fused_max_ok"] = group.transform_reduce(None, "max", "identity", xi0).item() == max(m.item() for m in mx)
+    torch.cuda.synchronize()
+    group.close()
+
     # dot fp64 and int32 min/max
     a = torch.rand(e - b, dtype=torch.float64, device=dev)
     c = torch.rand(e - b, dtype=torch.float64, device=dev)
