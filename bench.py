@@ -301,8 +301,11 @@ def bench_parts(torch, algo, dev, args, peak):
     n = 1 << 25
     a, b, c = (torch.empty(n, dtype=torch.float64, device=dev) for _ in range(3))
     algo.babelstream("init", a, b, c)
-    measure("triad_f64_2^25", lambda: algo.babelstream("triad", a, b, c), 3 * 8 * n)
+    # BabelStream byte accounting (babelStreamCommon.hpp:440-463): copy/mul/dot move 2 arrays, add/triad 3
     measure("copy_f64_2^25", lambda: algo.babelstream("copy", a, b, c), 2 * 8 * n)
+    measure("mul_f64_2^25", lambda: algo.babelstream("mul", a, b, c), 2 * 8 * n)
+    measure("add_f64_2^25", lambda: algo.babelstream("add", a, b, c), 3 * 8 * n)
+    measure("triad_f64_2^25", lambda: algo.babelstream("triad", a, b, c), 3 * 8 * n)
     out = torch.empty(1, dtype=torch.float64, device=dev)
     measure("dot_f64_2^25", lambda: algo.transform_reduce(0.0, out, "plus", "product", a, b), 2 * 8 * n)
     del a, b, c
@@ -318,6 +321,39 @@ def bench_parts(torch, algo, dev, args, peak):
     yu = torch.empty_like(xu)
     measure("inclusive_scan_u64_2^28", lambda: algo.inclusive_scan(yu, xu), 2 * 8 * n)
     del xu, yu
+
+    # nBody, 262144 bodies, one step = kick + drift; 20 flop per pair (example/nBody/src/common.hpp:21-30)
+    nb = 262144
+    m, px, py, pz = (torch.empty(nb, dtype=torch.float32, device=dev) for _ in range(4))
+    algo.random_f32(m, SEED + 1, 0.5, 1.0)
+    for k, t in enumerate((px, py, pz)):
+        algo.random_f32(t, SEED + 2 + k, 0.0, 1.0)
+    v = [torch.zeros(nb, dtype=torch.float32, device=dev) for _ in range(3)]
+    flops = 20.0 * nb * nb + 6.0 * nb
+    ms_nb, kern_nb = time_steps(torch, False, lambda ev: _wrap(torch, ev, lambda: algo.nbody_step(
+        m, px, py, pz, *v, 1e-3, 1e-3)), 10, 2)
+    fp32_peak = 148 * 128 * 2 * 1.965e9
+    parts["nbody_262144_step"] = {"GFLOP/s": round(flops / (kern_nb * 1e-3) / 1e9, 1),
+                                  "frac_fp32_fma": round(flops / (kern_nb * 1e-3) / fp32_peak, 4),
+                                  "kernel_ms": round(kern_nb, 4), "flop_per_step": flops, "steps": 10,
+                                  "peak": "148 SMs x 128 FP32 lanes x 2 x 1.965 GHz = 74.4 TFLOP/s (nominal)"}
+    del m, px, py, pz, v
+
+    # heat, 32768 x 32768 interior fp64 (8.6 GB per field), dt/dx^2 = 0.2
+    side = 32768
+    u = torch.empty((side + 2, side + 2), dtype=torch.float64, device=dev)
+    dx = 1.0 / (side + 1)
+    algo.heat_init(u, dx, dx)
+    w = u.clone()
+    cells = float(side) * side
+    state = [u, w]
+
+    def heat_step():
+        algo.heat_step(state[0], state[1], 0.2, 0.2)
+        state[0], state[1] = state[1], state[0]
+
+    measure("heat_32768^2_step", heat_step, 16.0 * cells)
+    del u, w, state
     torch.cuda.synchronize()
     return parts
 
