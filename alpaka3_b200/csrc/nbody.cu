@@ -4,12 +4,12 @@
 // functor run through onHost::concurrent (Kernels.hpp:126-142, nBody.cpp:196-205).
 //
 // Per pair (i, j): d = p_j - p_i; r2 = |d|^2 + eps; inv = rsqrt(r2^3); a_i += m_j * inv * d. Not a dense contraction,
-// so no tensor cores: the pair math is 12 FP32 lane operations plus one MUFU rsqrt. Each thread keeps 4 i-bodies in
-// registers as two packed pairs and evaluates them with the sm_100 packed FP32x2 instructions (__fadd2_rn,
+// so no tensor cores: the pair math is 12 FP32 lane operations plus one MUFU rsqrt. Each thread keeps 6 i-bodies in
+// registers as three packed pairs and evaluates them with the sm_100 packed FP32x2 instructions (__fadd2_rn,
 // __fmul2_rn, __ffma2_rn), which halves the issue slots of the FP32 work and leaves room for the MUFU and the shared
-// memory broadcast of each j-body (one 16-byte LDS per j for 4 pairs).
+// memory broadcast of each j-body (one 16-byte LDS per j for 6 pairs).
 //
-// Work split: items = (block of 512 i-bodies) x (slice of the j range). A resident grid pulls items from an atomic
+// Work split: items = (block of 768 i-bodies) x (slice of the j range). A resident grid pulls items from an atomic
 // counter (dynamic balance across the 148 SMs) and writes per-slice partial accelerations; a second kernel sums the
 // slices in fixed order, applies v += a*dt and optionally x += v*dt, so results do not depend on scheduling.
 #include "common.cuh"
@@ -18,11 +18,28 @@ namespace a3b
 {
     namespace
     {
-        constexpr int kThreads = 128;
-        constexpr int kPerThread = 4;
-        constexpr int kIBlock = kThreads * kPerThread; // 512 i-bodies per item
+#ifndef A3B_NBODY_PAIRS
+#define A3B_NBODY_PAIRS 3
+#endif
+#ifndef A3B_NBODY_THREADS
+#define A3B_NBODY_THREADS 128
+#endif
+        constexpr int kThreads = A3B_NBODY_THREADS;
+        constexpr int kPairs = A3B_NBODY_PAIRS;         // packed i-body pairs per thread
+        constexpr int kPerThread = 2 * kPairs;
+        constexpr int kIBlock = kThreads * kPerThread; // i-bodies per work item
         constexpr int kJTile = 512;                    // j-bodies staged in shared memory per step
         constexpr float kFar = 1.0e15f;                // padding body: far away and massless => contributes 0
+
+        // Reciprocal square root as the single PTX instruction rsqrt.approx.ftz.f32 (one MUFU operation; the
+        // library rsqrtf adds denormal handling around it, which cost 20% of the pair throughput here). Arguments are
+        // r^6 with r^2 >= eps > 0, far above the denormal range; the parity tests bound the effect on positions.
+        __device__ __forceinline__ float rsqrtApprox(float x)
+        {
+            float r;
+            asm("rsqrt.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
+            return r;
+        }
 
         struct NbHeader
         {
@@ -67,11 +84,11 @@ namespace a3b
                 unsigned const iblk = item / slices;
                 unsigned const slice = item - iblk * slices;
 
-                // i-bodies of this thread: local index li = iblk*512 + threadIdx.x + k*128
-                float2 nxi[2], nyi[2], nzi[2]; // negated positions, packed pairs (k=0,1) and (k=2,3)
-                float2 ax[2], ay[2], az[2];
+                // i-bodies of this thread: local index li = iblk*kIBlock + threadIdx.x + k*kThreads
+                float2 nxi[kPairs], nyi[kPairs], nzi[kPairs]; // negated positions, packed pairs (2p, 2p+1)
+                float2 ax[kPairs], ay[kPairs], az[kPairs];
 #pragma unroll
-                for(int p = 0; p < 2; ++p)
+                for(int p = 0; p < kPairs; ++p)
                 {
                     float px[2], py[2], pz[2];
 #pragma unroll
@@ -112,7 +129,7 @@ namespace a3b
                         float2 const bz = make_float2(b.z, b.z);
                         float2 const bm = make_float2(b.w, b.w);
 #pragma unroll
-                        for(int p = 0; p < 2; ++p)
+                        for(int p = 0; p < kPairs; ++p)
                         {
                             float2 const dx = __fadd2_rn(bx, nxi[p]);
                             float2 const dy = __fadd2_rn(by, nyi[p]);
@@ -121,7 +138,7 @@ namespace a3b
                             r2 = __ffma2_rn(dy, dy, r2);
                             r2 = __ffma2_rn(dx, dx, r2);
                             float2 const r6 = __fmul2_rn(__fmul2_rn(r2, r2), r2);
-                            float2 const inv = make_float2(rsqrtf(r6.x), rsqrtf(r6.y));
+                            float2 const inv = make_float2(rsqrtApprox(r6.x), rsqrtApprox(r6.y));
                             float2 const s = __fmul2_rn(bm, inv);
                             ax[p] = __ffma2_rn(s, dx, ax[p]);
                             ay[p] = __ffma2_rn(s, dy, ay[p]);
@@ -132,7 +149,7 @@ namespace a3b
 
                 float* const px = partial + static_cast<uint64_t>(slice) * 3u * partialStride;
 #pragma unroll
-                for(int p = 0; p < 2; ++p)
+                for(int p = 0; p < kPairs; ++p)
 #pragma unroll
                     for(int h = 0; h < 2; ++h)
                     {
