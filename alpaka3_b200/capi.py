@@ -60,6 +60,7 @@ SIGNATURES = {
     "a3b_peer_group_connect": [_P, _P],
     "a3b_peer_group_destroy": [_P],
     "a3b_transform_reduce_allranks": [_P, _P, _I, _I, _I, _P, _P, _U64, _P, _P],
+    "a3b_reduce_lower_ranks": [_P, _P, _I, _P, _U64, _P],
     "a3b_scan_buffer_size": [_I, _U64],
     "a3b_scan": [_P, _I, _I, _P, _P, _U64, _P, _P, ctypes.c_size_t],
     "a3b_scan_debug_stall": [_P, _I, _P, _P, _U64, _U64],

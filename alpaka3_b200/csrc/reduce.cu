@@ -367,6 +367,8 @@ namespace a3b
         // Local reduction as reduceKernel; the last block then stores the unrounded local total into slot
         // [epoch parity][rank] of every rank's slot buffer (value, then the epoch with release semantics), waits for
         // the world's values in its own buffer and combines them in rank order: every rank computes the same bits.
+        // With lowerRanksOnly the combination covers ranks 0 .. rank-1 (the carry of a scan split across ranks); the
+        // wait still covers every rank, so one call's slots are never overwritten by the next call too early.
         template<typename T, int W, int ROp, int XOp>
         __global__ void __launch_bounds__(kBlock) reduceAllRanksKernel(
             T const* __restrict__ in0,
@@ -377,6 +379,7 @@ namespace a3b
             ReduceScratch* scratch,
             typename AccOf<T, ROp>::type* partials,
             PeerSlots peers,
+            bool lowerRanksOnly,
             unsigned* errWord,
             uint64_t timeoutNs)
         {
@@ -428,7 +431,7 @@ namespace a3b
                     }
                     __nanosleep(32);
                 }
-                if(ok)
+                if(ok && (!lowerRanksOnly || q < peers.rank))
                 {
                     unsigned long long const vb = ldRelaxedSys(slot);
                     A val;
@@ -442,7 +445,8 @@ namespace a3b
         }
 
         template<typename T, int W, int ROp, int XOp>
-        int launchAllRanks(cudaStream_t s, a3b_peer_group* g, T const* in0, T const* in1, uint64_t n, T neutral, void* out)
+        int launchAllRanks(cudaStream_t s, a3b_peer_group* g, T const* in0, T const* in1, uint64_t n, T neutral, void* out,
+                           bool lower)
         {
             using A = typename AccOf<T, ROp>::type;
             DeviceProps const* props = nullptr;
@@ -471,13 +475,15 @@ namespace a3b
                 return rc;
             auto* hdr = static_cast<ReduceScratch*>(scr);
             reduceAllRanksKernel<T, W, ROp, XOp><<<grid, kBlock, 0, s>>>(
-                in0, in1, n, neutral, out, hdr, reinterpret_cast<A*>(hdr + 1), peers, props->errWord, waitTimeoutNs());
+                in0, in1, n, neutral, out, hdr, reinterpret_cast<A*>(hdr + 1), peers, lower, props->errWord,
+                waitTimeoutNs());
             A3B_CHECK_LAUNCH("transform_reduce_allranks launch");
             return A3B_OK;
         }
 
         template<typename T, int ROp, int XOp>
-        int allRanksLayout(cudaStream_t s, a3b_peer_group* g, T const* in0, T const* in1, uint64_t n, T neutral, void* out)
+        int allRanksLayout(cudaStream_t s, a3b_peer_group* g, T const* in0, T const* in1, uint64_t n, T neutral, void* out,
+                           bool lower)
         {
             auto al = [&](uintptr_t a)
             {
@@ -486,24 +492,25 @@ namespace a3b
             };
             constexpr int W = 16 / sizeof(T);
             if(al(32))
-                return launchAllRanks<T, 2 * W, ROp, XOp>(s, g, in0, in1, n, neutral, out);
+                return launchAllRanks<T, 2 * W, ROp, XOp>(s, g, in0, in1, n, neutral, out, lower);
             if(al(16))
-                return launchAllRanks<T, W, ROp, XOp>(s, g, in0, in1, n, neutral, out);
-            return launchAllRanks<T, 1, ROp, XOp>(s, g, in0, in1, n, neutral, out);
+                return launchAllRanks<T, W, ROp, XOp>(s, g, in0, in1, n, neutral, out, lower);
+            return launchAllRanks<T, 1, ROp, XOp>(s, g, in0, in1, n, neutral, out, lower);
         }
 
         template<typename T, int ROp>
-        int allRanksXform(cudaStream_t s, a3b_peer_group* g, int xop, T const* in0, T const* in1, uint64_t n, T neutral, void* out)
+        int allRanksXform(cudaStream_t s, a3b_peer_group* g, int xop, T const* in0, T const* in1, uint64_t n, T neutral, void* out,
+                          bool lower)
         {
             switch(xop)
             {
             case A3B_XFORM_IDENTITY:
-                return allRanksLayout<T, ROp, A3B_XFORM_IDENTITY>(s, g, in0, in1, n, neutral, out);
+                return allRanksLayout<T, ROp, A3B_XFORM_IDENTITY>(s, g, in0, in1, n, neutral, out, lower);
             case A3B_XFORM_SQUARE:
-                return allRanksLayout<T, ROp, A3B_XFORM_SQUARE>(s, g, in0, in1, n, neutral, out);
+                return allRanksLayout<T, ROp, A3B_XFORM_SQUARE>(s, g, in0, in1, n, neutral, out, lower);
             case A3B_XFORM_PRODUCT:
                 A3B_REQUIRE(in1, "product transform needs two inputs");
-                return allRanksLayout<T, ROp, A3B_XFORM_PRODUCT>(s, g, in0, in1, n, neutral, out);
+                return allRanksLayout<T, ROp, A3B_XFORM_PRODUCT>(s, g, in0, in1, n, neutral, out, lower);
             default:
                 setError("unknown transform op %d", xop);
                 return A3B_ERR_INVALID;
@@ -512,7 +519,7 @@ namespace a3b
 
         template<typename T>
         int allRanksReduce(cudaStream_t s, a3b_peer_group* g, int rop, int xop, void const* in0, void const* in1, uint64_t n,
-                           void const* neutral, void* out)
+                           void const* neutral, void* out, bool lower = false)
         {
             T const nv = *static_cast<T const*>(neutral);
             auto i0 = static_cast<T const*>(in0);
@@ -520,11 +527,11 @@ namespace a3b
             switch(rop)
             {
             case A3B_REDUCE_PLUS:
-                return allRanksXform<T, A3B_REDUCE_PLUS>(s, g, xop, i0, i1, n, nv, out);
+                return allRanksXform<T, A3B_REDUCE_PLUS>(s, g, xop, i0, i1, n, nv, out, lower);
             case A3B_REDUCE_MIN:
-                return allRanksXform<T, A3B_REDUCE_MIN>(s, g, xop, i0, i1, n, nv, out);
+                return allRanksXform<T, A3B_REDUCE_MIN>(s, g, xop, i0, i1, n, nv, out, lower);
             case A3B_REDUCE_MAX:
-                return allRanksXform<T, A3B_REDUCE_MAX>(s, g, xop, i0, i1, n, nv, out);
+                return allRanksXform<T, A3B_REDUCE_MAX>(s, g, xop, i0, i1, n, nv, out, lower);
             default:
                 setError("unknown reduce op %d", rop);
                 return A3B_ERR_INVALID;
@@ -911,6 +918,35 @@ extern "C"
             return allRanksReduce<float>(s, group, reduce_op, transform_op, in0, in1, n, neutral, out);
         case A3B_F64:
             return allRanksReduce<double>(s, group, reduce_op, transform_op, in0, in1, n, neutral, out);
+        default:
+            setError("unknown dtype %d", dtype);
+            return A3B_ERR_INVALID;
+        }
+    }
+
+    int a3b_reduce_lower_ranks(a3b_stream_t stream, a3b_peer_group* group, int dtype, void const* in, uint64_t n,
+                               void* carry_out)
+    {
+        A3B_REQUIRE(group && carry_out, "null group/out");
+        A3B_REQUIRE(in || n == 0, "null input");
+        auto s = static_cast<cudaStream_t>(stream);
+        int64_t const zero = 0;
+        double const zf = 0.0;
+        float const zf32 = 0.f;
+        switch(dtype)
+        {
+        case A3B_I32:
+            return allRanksReduce<int32_t>(s, group, A3B_REDUCE_PLUS, A3B_XFORM_IDENTITY, in, nullptr, n, &zero, carry_out, true);
+        case A3B_U32:
+            return allRanksReduce<uint32_t>(s, group, A3B_REDUCE_PLUS, A3B_XFORM_IDENTITY, in, nullptr, n, &zero, carry_out, true);
+        case A3B_I64:
+            return allRanksReduce<int64_t>(s, group, A3B_REDUCE_PLUS, A3B_XFORM_IDENTITY, in, nullptr, n, &zero, carry_out, true);
+        case A3B_U64:
+            return allRanksReduce<uint64_t>(s, group, A3B_REDUCE_PLUS, A3B_XFORM_IDENTITY, in, nullptr, n, &zero, carry_out, true);
+        case A3B_F32:
+            return allRanksReduce<float>(s, group, A3B_REDUCE_PLUS, A3B_XFORM_IDENTITY, in, nullptr, n, &zf32, carry_out, true);
+        case A3B_F64:
+            return allRanksReduce<double>(s, group, A3B_REDUCE_PLUS, A3B_XFORM_IDENTITY, in, nullptr, n, &zf, carry_out, true);
         default:
             setError("unknown dtype %d", dtype);
             return A3B_ERR_INVALID;

@@ -269,3 +269,13 @@ class PeerGroup:
                   algo.XFORM[transform_fn], algo._ptr(in0_local), algo._ptr(in1_local), in0_local.numel(), p,
                   algo._ptr(out))
         return out
+
+    def scan(self, inclusive, out_local, data_local, carry=None):
+        """Scan of a contiguously sharded array in two launches per rank and no NCCL: the shard total and the
+        exclusive carry over lower ranks come from one fused kernel (peer slots), then the carried single-pass scan."""
+        from . import algo, capi
+        if carry is None:
+            carry = torch.empty(1, dtype=data_local.dtype, device=data_local.device)
+        capi.call("a3b_reduce_lower_ranks", algo.stream_handle(), self.g, algo.dtype_code(data_local),
+                  algo._ptr(data_local), data_local.numel(), algo._ptr(carry))
+        return algo._scan(inclusive, out_local, data_local, None, carry)

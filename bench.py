@@ -482,6 +482,131 @@ def run_profile_case(args):
     print(json.dumps({"profile_case": case, "n_log2": lg, "kernel_ms": kern, "units_per_s": nbytes / (kern * 1e-3)}))
 
 
+def run_workload(args):
+    """The other configurations of the metric on N ranks (one JSON line from rank 0, same keys as the headline):
+    triad / dot (BabelStream fp64, 2^25 elements per array PER GPU: weak scaling, so every rank's arrays exceed L2),
+    scan_i32 (exclusive scan of 2^30 int32 split across ranks, reduce + all-gather of totals + carried scan),
+    scan_u64 (inclusive scan of 2^28 uint64, likewise), nbody (262144 bodies split across ranks, all-gather of
+    positions each step), heat (32768^2 grid in row slabs, halo rows exchanged each step, overlapped)."""
+    import torch
+    from alpaka3_b200 import algo, dist as adist
+    world, rank, local = adist.init()
+    dist_on = world > 1
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    peak, peak_kind = peaks()
+    wl = args.workload
+    s = torch.cuda.current_stream()
+    launches = [0]
+    scaling = "strong"
+    if wl in ("triad", "dot"):
+        n = 1 << 25
+        a, b, c = (torch.empty(n, dtype=torch.float64, device=dev) for _ in range(3))
+        algo.babelstream("init", a, b, c)
+        out = torch.empty(1, dtype=torch.float64, device=dev)
+        scaling = "weak"
+        if wl == "triad":
+            fn, unit_bytes = (lambda: algo.babelstream("triad", a, b, c)), 24.0 * n
+        else:
+            group = adist.PeerGroup() if dist_on else None  # noqa: F841 - closed after the timing
+            fn = (lambda: group.transform_reduce(0.0, "plus", "product", a, b, out=out)) if group else (
+                lambda: algo.transform_reduce(0.0, out, "plus", "product", a, b))
+            unit_bytes = 16.0 * n
+        total = unit_bytes * world
+        desc = f"BabelStream {wl} fp64, 2^25 elements per array on each GPU (weak scaling)"
+        metric_unit = "GB/s"
+    elif wl in ("scan_i32", "scan_u64"):
+        n = (1 << 30) if wl == "scan_i32" else (1 << 28)
+        dt = torch.int32 if wl == "scan_i32" else torch.int64
+        b0, e0 = adist.shard_range(n, rank, world)
+        x = torch.empty(e0 - b0, dtype=dt, device=dev)
+        if wl == "scan_i32":
+            algo.random_u32(x, SEED, start=b0, shift=28)
+        else:
+            algo.random_u64(x, SEED, start=b0)
+        y = torch.empty_like(x)
+        group = adist.PeerGroup() if dist_on else None  # noqa: F841 - closed after the timing
+        incl = wl != "scan_i32"
+        fn = (lambda: group.scan(incl, y, x)) if group else (lambda: algo._scan(incl, y, x))
+        unit_bytes = 2.0 * x.element_size() * (e0 - b0)
+        total = 2.0 * x.element_size() * n
+        desc = (f"{'exclusive' if wl == 'scan_i32' else 'inclusive'} scan of 2^{30 if wl == 'scan_i32' else 28} "
+                f"{'int32 in [0,16)' if wl == 'scan_i32' else 'uint64'} split across ranks (one fused launch for the "
+                "shard total and the carry over lower ranks via peer slots, then the carried single-pass scan)")
+        metric_unit = "GB/s"
+    elif wl == "nbody":
+        nb = 262144
+        m, px, py, pz = (torch.empty(nb, dtype=torch.float32, device=dev) for _ in range(4))
+        algo.random_f32(m, SEED + 1, 0.5, 1.0)
+        for k, t in enumerate((px, py, pz)):
+            algo.random_f32(t, SEED + 2 + k, 0.0, 1.0)
+        b0, e0 = adist.shard_range(nb, rank, world)
+        v = [torch.zeros(e0 - b0, dtype=torch.float32, device=dev) for _ in range(3)]
+        sim = adist.NBody(m, px, py, pz, *v, b0)
+        fn = lambda: sim.step(1e-3, 1e-3)  # noqa: E731
+        unit_bytes = 20.0 * (e0 - b0) * nb
+        total = 20.0 * nb * nb + 6.0 * nb
+        desc = "all-pairs nBody, 262144 fp32 bodies split across ranks, positions all-gathered every step"
+        metric_unit = "GFLOP/s"
+    else:
+        side = 32768
+        hb, he = adist.shard_range(side, rank, world)
+        u = torch.empty((he - hb + 2, side + 2), dtype=torch.float64, device=dev)
+        dx = 1.0 / (side + 1)
+        algo.heat_init(u, dx, dx, row_offset=hb, global_rows=side)
+        w = u.clone()
+        slab = adist.HeatSlab(u, w, 0.2, 0.2)
+        fn = slab.step
+        unit_bytes = 16.0 * (he - hb) * side
+        total = 16.0 * side * side
+        desc = "heat 5-point stencil, 32768^2 fp64 in row slabs, one halo row exchanged with each neighbour per step"
+        metric_unit = "GB/s"
+
+    def step(ev):
+        if ev:
+            ev[0].record(s)
+        fn()
+        if ev:
+            ev[1].record(s)
+            launches[0] += 1
+
+    sampler = ClockSampler(pci_bus_id(torch, local))
+    sampler.start()
+    ms, kern = time_steps(torch, dist_on, step, args.steps, args.warmup)
+    sampler.stop()
+    if wl == "heat":
+        slab.finish()
+    ms = max_over_ranks(torch, dist_on, ms)
+    kern = max_over_ranks(torch, dist_on, kern)
+    scale = 1e9
+    value = total / (ms * 1e-3) / scale
+    per_gpu = unit_bytes / (kern * 1e-3) / scale
+    if metric_unit == "GFLOP/s":
+        fp32_peak = 148 * 128 * 2 * 1.965e9 / 1e9
+        roof = {"bound": "fp32 pipe", "achieved": round(per_gpu, 1), "peak": round(fp32_peak, 1), "unit": "GFLOP/s",
+                "frac": round(per_gpu / fp32_peak, 4), "peak_kind": "nominal (148 SMs x 128 lanes x 2 x 1.965 GHz)"}
+    else:
+        roof = {"bound": "hbm", "achieved": round(per_gpu, 1), "peak": peak, "unit": "GB/s",
+                "frac": round(per_gpu / peak, 4), "peak_kind": peak_kind}
+    roof["step_ms_per_rank"] = round(kern, 5)
+    if rank == 0:
+        line = {"metric": METRIC, "value": round(value, 2), "unit": metric_unit, "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": round(ms, 5), "higher_is_better": True, "scaling": scaling,
+                "vs_baseline": None, "dtype": {"triad": "f64", "dot": "f64", "scan_i32": "int32", "scan_u64": "uint64",
+                                               "nbody": "f32", "heat": "f64"}[wl],
+                "data": "synthetic (seeded Philox4x32-10)", "config": {"workload": desc, "name": wl},
+                "roofline": roof, "gpu_launches": launches[0], "clocks": sampler.summary()}
+        print(json.dumps(line), flush=True)
+    if dist_on:
+        import torch.distributed as dist
+        torch.cuda.synchronize()
+        dist.barrier()
+        if wl in ("dot", "scan_i32", "scan_u64") and group is not None:
+            group.close()
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -492,6 +617,9 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=8.0)
+    ap.add_argument("--workload", default="sumsq",
+                    choices=["sumsq", "triad", "dot", "scan_i32", "scan_u64", "nbody", "heat"],
+                    help="sumsq is the headline; the others time the remaining configurations on N ranks")
     ap.add_argument("--collective", default="fused", choices=["fused", "nccl"],
                     help="N > 1: combine the per-rank partials inside the reduction kernel over mapped peer memory "
                          "(fused) or with an NCCL all-reduce after it")
@@ -506,6 +634,8 @@ def main():
         run_reference(args)
     elif args.profile_case:
         run_profile_case(args)
+    elif args.workload != "sumsq":
+        run_workload(args)
     else:
         run_b200(args)
 

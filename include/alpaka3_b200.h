@@ -206,6 +206,12 @@ A3B_API int a3b_transform_reduce_allranks(a3b_stream_t stream, a3b_peer_group* g
                                           int transform_op, void const* in0, void const* in1, uint64_t n,
                                           void const* neutral, void* out);
 
+/* Carry of a scan split across the ranks of a peer group: sums this rank's shard in one launch, exchanges the shard
+ * totals through the peer slots and writes sum(totals of ranks 0 .. rank-1) to carry_out (device pointer, one
+ * element of dtype; integers wrap). Feed it to a3b_scan as carry_in. */
+A3B_API int a3b_reduce_lower_ranks(a3b_stream_t stream, a3b_peer_group* group, int dtype, void const* in, uint64_t n,
+                                   void* carry_out);
+
 /* ------------------------------------------------------------------------------------------------------ scan */
 
 /* onHost::getScanBufferSize<T>(extents) (include/alpaka/onHost/algo/scan.hpp:26-30): bytes of the caller buffer that

@@ -40,6 +40,14 @@ def main():
     mx = [torch.zeros(1, dtype=torch.int32, device=dev) for _ in range(world)]
     torch.distributed.all_gather(mx, xi0.max().reshape(1))
     res["fused_max_ok"] = group.transform_reduce(None, "max", "identity", xi0).item() == max(m.item() for m in mx)
+    # scan carried through the peer slots (no NCCL)
+    xs0 = torch.empty(e - b, dtype=torch.int32, device=dev)
+    algo.random_u32(xs0, SEED, start=b, shift=1)  # large values: the carry wraps int32
+    ys0 = torch.empty_like(xs0)
+    for _ in range(3):
+        group.scan(False, ys0, xs0)
+    want0 = port.scan(port.gen_u32(n, shift=1), False)[b:e]
+    res["peer_scan_ok"] = bool((ys0.cpu().numpy().view(np.uint32) == want0).all())
     torch.cuda.synchronize()
     group.close()
 
