@@ -403,25 +403,30 @@ namespace a3b
             for(unsigned b = threadIdx.x; b < gridDim.x; b += kBlock)
                 r = combine<A, ROp>(r, __ldcg(partials + b));
             r = blockReduce<A, ROp>(r, smem);
-            if(threadIdx.x != 0)
+            if(threadIdx.x >= 32)
                 return;
-            scratch->ticket = 0u;
+            // warp 0: lane q exchanges with rank q (all ranks in parallel, one system-scope fence per lane)
+            int const lane = threadIdx.x;
+            if(lane == 0)
+                scratch->ticket = 0u;
             static_assert(sizeof(A) <= 8, "partials are exchanged as 8-byte words");
             unsigned long long bits = 0;
             memcpy(&bits, &r, sizeof(A));
             unsigned const par = peers.epoch & 1u;
-            for(int q = 0; q < peers.world; ++q)
+            bool const active = lane < peers.world;
+            if(active)
             {
-                unsigned long long* slot = peers.slots[q] + 2 * (par * kMaxPeers + peers.rank);
+                unsigned long long* slot = peers.slots[lane] + 2 * (par * kMaxPeers + peers.rank);
                 stRelaxedSys(slot, bits);
-                stReleaseSys(slot + 1, peers.epoch);
+                __threadfence_system(); // the value is visible to rank `lane` before the epoch that announces it
+                stRelaxedSys(slot + 1, peers.epoch);
             }
-            A total = neutralA;
             bool ok = true;
-            uint64_t const t0 = globalTimerNs();
-            for(int q = 0; q < peers.world && ok; ++q)
+            unsigned long long vb = 0;
+            if(active)
             {
-                unsigned long long const* slot = peers.slots[peers.rank] + 2 * (par * kMaxPeers + q);
+                unsigned long long const* slot = peers.slots[peers.rank] + 2 * (par * kMaxPeers + lane);
+                uint64_t const t0 = globalTimerNs();
                 while(ldAcquireSys(slot + 1) != peers.epoch)
                 {
                     if(globalTimerNs() - t0 > timeoutNs)
@@ -429,17 +434,27 @@ namespace a3b
                         ok = false;
                         break;
                     }
-                    __nanosleep(32);
+                    __nanosleep(20);
                 }
-                if(ok && (!lowerRanksOnly || q < peers.rank))
+                if(ok)
+                    vb = ldRelaxedSys(slot);
+            }
+            bool const allOk = __all_sync(0xffffffffu, ok);
+            // combine in rank order on lane 0: every rank gets the same bits
+            A total = neutralA;
+            for(int q = 0; q < peers.world; ++q)
+            {
+                unsigned long long const w = __shfl_sync(0xffffffffu, vb, q);
+                if(!lowerRanksOnly || q < peers.rank)
                 {
-                    unsigned long long const vb = ldRelaxedSys(slot);
                     A val;
-                    memcpy(&val, &vb, sizeof(A));
+                    memcpy(&val, &w, sizeof(A));
                     total = combine<A, ROp>(total, val);
                 }
             }
-            if(!ok)
+            if(lane != 0)
+                return;
+            if(!allOk)
                 atomicOr(errWord, kErrTimeout);
             writeResult<T, A>(out, total, false);
         }
