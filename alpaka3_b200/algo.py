@@ -228,3 +228,31 @@ def heat_init(u, dx, dy, row_offset=0, global_rows=None, stream=None):
         global_rows = rows
     capi.call("a3b_heat_init", stream_handle(stream), ctypes.c_void_p(u.data_ptr()), rows, cols, u.stride(0),
               row_offset, global_rows, float(dx), float(dy))
+
+
+def heat_exact(u, t, dx, dy, ring_only=False, row_offset=0, global_rows=None, stream=None):
+    """The heatEquation2D example's exact solution at time t on every cell, or on the global ring only."""
+    rows, cols = u.shape[0] - 2, u.shape[1] - 2
+    if global_rows is None:
+        global_rows = rows
+    capi.call("a3b_heat_exact", stream_handle(stream), ctypes.c_void_p(u.data_ptr()), rows, cols, u.stride(0),
+              row_offset, global_rows, float(t), float(dx), float(dy), 1 if ring_only else 0)
+
+
+def heat_problem(n, steps, t_max, device, stream=None):
+    """Runs the heatEquation2D example's own problem (heatEquation2D.cpp:97-196) on the device: exact initial field,
+    `steps` Jacobi steps with the exact solution re-imposed on the ring after each; returns the final field."""
+    extent = n + 2
+    dx = 1.0 / (extent - 1)
+    dy = 1.0 / (extent - 1)
+    dt = t_max / steps
+    rX = dt / (dx * dx)
+    rY = dt / (dy * dy)
+    cur = torch.empty((extent, extent), dtype=torch.float64, device=device)
+    heat_exact(cur, 0.0, dx, dy, stream=stream)
+    nxt = cur.clone()
+    for step in range(1, steps + 1):
+        heat_step(cur, nxt, rX, rY, stream=stream)
+        heat_exact(nxt, float(step) * dt, dx, dy, ring_only=True, stream=stream)
+        cur, nxt = nxt, cur
+    return cur

@@ -68,6 +68,7 @@ SIGNATURES = {
     "a3b_nbody_step": [_P, _P, _P, _P, _P, _U64, _U64, _U64, _P, _P, _P, _F, _F],
     "a3b_heat_step": [_P, _P, _P, _U64, _U64, _U64, _U64, _U64, _D, _D],
     "a3b_heat_init": [_P, _P, _U64, _U64, _U64, _U64, _U64, _D, _D],
+    "a3b_heat_exact": [_P, _P, _U64, _U64, _U64, _U64, _U64, _D, _D, _D, _I],
 }
 _RESTYPES = {"a3b_last_error": ctypes.c_char_p, "a3b_scan_buffer_size": ctypes.c_size_t,
              "a3b_ipc_handle_size": ctypes.c_size_t}

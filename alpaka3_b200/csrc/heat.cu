@@ -164,6 +164,36 @@ namespace a3b
                 v = sin(CUDART_PI * (static_cast<double>(c) * dx)) * sin(CUDART_PI * (static_cast<double>(gr) * dy));
             u[r * pitch + c] = v;
         }
+        // Exact solution of the heatEquation2D example, e^{-pi^2 t} (sin pi x + sin pi y) (analyticalSolution.hpp:17-21),
+        // at x = col*dx, y = global_row*dy: on every cell (initial field) or on the global ring only (the example's
+        // time-dependent Dirichlet boundary, BoundaryKernel.hpp:23-57).
+        __global__ void __launch_bounds__(kThreads) heatExactKernel(
+            double* u,
+            uint64_t rows,
+            uint64_t cols,
+            uint64_t pitch,
+            uint64_t rowOffset,
+            uint64_t globalRows,
+            double t,
+            double dx,
+            double dy,
+            bool ringOnly)
+        {
+            uint64_t const c = static_cast<uint64_t>(blockIdx.x) * kThreads + threadIdx.x;
+            double const decay = exp(-CUDART_PI * CUDART_PI * t);
+            for(uint64_t r = blockIdx.y; r < rows + 2u; r += gridDim.y)
+            {
+                if(c >= cols + 2u)
+                    return;
+                uint64_t const gr = r + rowOffset;
+                bool const ring = gr == 0u || gr == globalRows + 1u || c == 0u || c == cols + 1u;
+                if(ringOnly && !ring)
+                    continue;
+                double const x = static_cast<double>(c) * dx;
+                double const y = static_cast<double>(gr) * dy;
+                u[r * pitch + c] = decay * (sin(CUDART_PI * x) + sin(CUDART_PI * y));
+            }
+        }
     } // namespace
 } // namespace a3b
 
@@ -213,6 +243,19 @@ extern "C"
         heatInitKernel<<<grid, kThreads, 0, static_cast<cudaStream_t>(stream)>>>(u, rows, cols, pitch_elems,
                                                                                   row_offset, global_rows, dx, dy);
         A3B_CHECK_LAUNCH("heat init launch");
+        return A3B_OK;
+    }
+
+    int a3b_heat_exact(a3b_stream_t stream, double* u, uint64_t rows, uint64_t cols, uint64_t pitch_elems,
+                       uint64_t row_offset, uint64_t global_rows, double t, double dx, double dy, int ring_only)
+    {
+        A3B_REQUIRE(u, "null grid pointer");
+        A3B_REQUIRE(pitch_elems >= cols + 2u, "pitch smaller than a row with its halo");
+        uint64_t const gy = rows + 2u < 65535u ? rows + 2u : 65535u;
+        dim3 const grid(static_cast<unsigned>((cols + 2u + kThreads - 1) / kThreads), static_cast<unsigned>(gy));
+        heatExactKernel<<<grid, kThreads, 0, static_cast<cudaStream_t>(stream)>>>(
+            u, rows, cols, pitch_elems, row_offset, global_rows, t, dx, dy, ring_only != 0);
+        A3B_CHECK_LAUNCH("heat exact launch");
         return A3B_OK;
     }
 }

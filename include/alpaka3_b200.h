@@ -262,6 +262,13 @@ A3B_API int a3b_heat_step(a3b_stream_t stream, double const* cur, double* next, 
 A3B_API int a3b_heat_init(a3b_stream_t stream, double* u, uint64_t rows, uint64_t cols, uint64_t pitch_elems,
                   uint64_t row_offset, uint64_t global_rows, double dx, double dy);
 
+/* The heatEquation2D example's own problem (example/heatEquation2D/src/analyticalSolution.hpp:17-78,
+ * BoundaryKernel.hpp:23-57): writes the exact solution e^{-pi^2 t}(sin pi x + sin pi y), x = col*dx, y = row*dy, to
+ * every cell (ring_only == 0, the initial field initalizeBuffer writes) or only to the cells on the global ring
+ * (ring_only != 0, the time-dependent Dirichlet boundary applied after each step). Grid as in a3b_heat_step. */
+A3B_API int a3b_heat_exact(a3b_stream_t stream, double* u, uint64_t rows, uint64_t cols, uint64_t pitch_elems,
+                           uint64_t row_offset, uint64_t global_rows, double t, double dx, double dy, int ring_only);
+
 #ifdef __cplusplus
 }
 #endif

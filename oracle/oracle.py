@@ -184,6 +184,8 @@ class Ref:
         L.ref_heat_steps.argtypes = [ctypes.c_int, _P, _P, _U32, _U32, ctypes.c_double, ctypes.c_double,
                                      ctypes.c_double]
         L.ref_nbody_steps.argtypes = [ctypes.c_int] + [_P] * 7 + [_U32, _U32, ctypes.c_float]
+        L.ref_heat_problem.argtypes = [ctypes.c_int, _U32, _U32, ctypes.c_double, _P]
+        L.ref_heat_problem.restype = ctypes.c_double
         L.ref_num_threads.restype = ctypes.c_int
 
     KERNELS = {"copy": 1, "mul": 2, "add": 4, "triad": 8, "dot": 16, "nstream": 32}
@@ -236,6 +238,12 @@ class Ref:
         rc = self.lib.ref_heat_steps(exec_kind, _p(cur), _p(nxt), n, steps, dx, dy, dt)
         assert rc == 0
         return cur
+
+    def heat_problem(self, n, steps, t_max, exec_kind=1):
+        """The heatEquation2D example's own problem; returns (final (n+2)^2 field, its validation error)."""
+        out = np.empty((n + 2, n + 2), dtype=np.float64)
+        err = self.lib.ref_heat_problem(exec_kind, n, steps, t_max, _p(out))
+        return out, err
 
     def nbody_steps(self, m, x, y, z, vx, vy, vz, dt, steps, exec_kind=1):
         """Reference step with its built-in softening EPS = 4 (example/nBody/src/common.hpp:41)."""

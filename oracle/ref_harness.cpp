@@ -10,6 +10,8 @@
  *   ref_reduce           include/alpaka/onHost/algo/reduce.hpp:28-79, test/unit/algorithm/reduce.cpp:135-152
  *   ref_scan             include/alpaka/onHost/algo/scan.hpp:45-218
  *   ref_heat_steps       example/heatEquation2D/src/StencilKernel.hpp:26-86 driven as heatEquation2D.cpp:134-196
+ *   ref_heat_problem     the example's own problem end to end: initalizeBuffer, StencilKernel + BoundaryKernel per
+ *                        step (heatEquation2D.cpp:97-196, BoundaryKernel.hpp:23-57, analyticalSolution.hpp:17-78)
  *   ref_nbody_steps      example/nBody/src/Kernels.hpp:24-142 driven as nBody.cpp:171-205 (EPS fixed at 4 there)
  * The BabelStream operation functors below are written here (they live in the reference's benchmark TU and cannot
  * be included); each states the same element-wise assignment as the reference op it mirrors.
@@ -21,9 +23,12 @@
 #include <cstring>
 #include <functional>
 #include <limits>
+#include <vector>
 
 // reference example kernels, included from their own location in the reference tree
+#include "BoundaryKernel.hpp"  // example/heatEquation2D/src
 #include "StencilKernel.hpp"   // example/heatEquation2D/src
+#include "analyticalSolution.hpp"
 #include "Kernels.hpp"         // example/nBody/src
 
 using namespace alpaka;
@@ -431,6 +436,53 @@ extern "C"
         if(steps % 2u == 1u)
             std::memcpy(cur, next, sizeof(double) * (n + 2u) * (n + 2u));
         return 0;
+    }
+
+    /** The heatEquation2D example's own problem: n x n interior (n a multiple of 16), `steps` steps up to tMax, exact
+     * solution e^{-pi^2 t}(sin pi x + sin pi y) as initial field and time-dependent Dirichlet ring. Writes the final
+     * (n+2)^2 field to `out` and returns the example's own validation error (max |u - exact| over the interior). */
+    double ref_heat_problem(int execKind, uint32_t n, uint32_t steps, double tMax, double* out)
+    {
+        using namespace alpaka::onHost;
+        if(n % 16u != 0u)
+            return -1.0;
+        auto& q = hostQueue();
+        using IdxVec = Vec<uint32_t, 2u>;
+        IdxVec const numNodes{n, n};
+        IdxVec const extent{n + 2u, n + 2u};
+        double const dx = 1.0 / static_cast<double>(extent[1] - 1);
+        double const dy = 1.0 / static_cast<double>(extent[0] - 1);
+        double const dt = tMax / static_cast<double>(steps);
+        std::vector<double> a((n + 2u) * (n + 2u)), b((n + 2u) * (n + 2u));
+        auto va = makeView(api::host, a.data(), extent);
+        auto vb = makeView(api::host, b.data(), extent);
+        initalizeBuffer(va, dx, dy);
+        constexpr auto chunk = CVec<uint32_t, 16u, 16u>{};
+        auto const smemExt = CVec<uint32_t, 18u, 18u>{};
+        IdxVec const numChunks{n / 16u, n / 16u};
+        auto const withHalo = numNodes + IdxVec{2u, 2u};
+        withExec(
+            execKind,
+            [&](auto ex)
+            {
+                auto spec = FrameSpec{numChunks, chunk, ex};
+                auto const longest = std::max(withHalo.y(), withHalo.x());
+                auto border = FrameSpec{Vec{longest / chunk.x()}, Vec{std::max(chunk.y(), chunk.x())}, ex};
+                StencilKernel sk;
+                BoundaryKernel bk;
+                auto cur = va;
+                auto nxt = vb;
+                for(uint32_t step = 1; step <= steps; ++step)
+                {
+                    q.enqueue(spec, KernelBundle{sk, cur, nxt, chunk, smemExt, numNodes, dx, dy, dt});
+                    q.enqueue(border, KernelBundle{bk, nxt, withHalo, step, dx, dy, dt});
+                    onHost::wait(q);
+                    std::swap(cur, nxt);
+                }
+                std::memcpy(out, cur.data(), sizeof(double) * (n + 2u) * (n + 2u));
+            });
+        auto check = makeView(api::host, out, extent);
+        return validateSolution(check, extent, dx, dy, tMax).second;
     }
 
     /** Runs `steps` of the reference nBody step (UpdateVelocitiesKernel with its built-in EPS, then UpdatePositions

@@ -12,6 +12,8 @@ The fixtures are small (hashes, scalars, a few KB of arrays) and are committed; 
   heat.npz            StencilKernel on a 64x64 interior, sin*sin start, 25 steps (dt = 0.2 dx^2)
   nbody.npz           UpdateVelocitiesKernel + UpdatePositions (built-in EPS = 4), 512 bodies, 3 steps, dt = 1e-3
   sumsq.json          transformReduce(plus, x*x) over 2^20 seeded fp32 in [-1, 1) (reference fp32 value)
+  heat_problem.npz    the heatEquation2D example's own problem at its defaults (64 x 64, 4000 steps, tMax 0.1: exact
+                      initial field, time-dependent Dirichlet ring): final field and the example's validation error
 """
 import hashlib
 import json
@@ -77,6 +79,8 @@ def main():
     x = port.gen_f32(1 << 20, -1.0, 1.0)
     json.dump({"n": 1 << 20, "seed": SEED, "ref_fp32": float(ref.sumsq(x)), "input_sha256": sha(x)},
               open(os.path.join(HERE, "sumsq.json"), "w"), indent=1)
+    u, err = ref.heat_problem(64, 4000, 0.1)
+    np.savez_compressed(os.path.join(HERE, "heat_problem.npz"), u=u, err=err, n=64, steps=4000, t_max=0.1)
     print("golden fixtures written to", HERE)
 
 

@@ -84,3 +84,22 @@ def test_heat_eigenmode_decay(cuda):
     want = u0 * lam ** steps
     err = (u - want).abs().max().item() / want.abs().max().item()
     assert err <= 1e-12
+
+
+def test_heat_example_problem_reference_golden(cuda):
+    """The heatEquation2D example end to end at its defaults (64 x 64, 4000 steps, tMax 0.1): exact initial field and
+    time-dependent Dirichlet ring (BoundaryKernel). Against the reference's own output (normwise 1e-12: the ring values
+    come from the device's exp/sin instead of the host's) and the example's own analytical check
+    (max error < 1e-4, example/heatEquation2D/src/analyticalSolution.hpp:31-56)."""
+    from alpaka3_b200 import algo
+    g = np.load(os.path.join(GOLDEN, "heat_problem.npz"))
+    n, steps, t_max = int(g["n"]), int(g["steps"]), float(g["t_max"])
+    u = algo.heat_problem(n, steps, t_max, cuda).cpu().numpy()
+    ref = g["u"]
+    assert np.max(np.abs(u - ref)) <= 1e-12 * np.max(np.abs(ref))
+    dx = 1.0 / (n + 1)
+    j, i = np.meshgrid(np.arange(n + 2), np.arange(n + 2))
+    exact = np.exp(-np.pi ** 2 * t_max) * (np.sin(np.pi * j * dx) + np.sin(np.pi * i * dx))
+    err = np.max(np.abs(u[1:-1, 1:-1] - exact[1:-1, 1:-1]))
+    assert err < 1e-4
+    assert abs(err - float(g["err"])) <= 1e-9

@@ -104,3 +104,12 @@ def test_reduce_matches_reference_nd(port, ref):
         x = port.gen_u32(int(np.prod(ext)), shift=1).astype(np.int32).reshape(ext)
         for op in ("plus", "min", "max"):
             assert ref.reduce(op, x) == port.reduce_int(op, x.ravel())
+
+
+def test_heat_example_problem_golden(ref):
+    """The heatEquation2D example's own problem through alpaka3's host backend reproduces the fixture and passes the
+    example's analytical check (max error < 1e-4)."""
+    g = np.load(os.path.join(GOLDEN, "heat_problem.npz"))
+    u, err = ref.heat_problem(int(g["n"]), int(g["steps"]), float(g["t_max"]))
+    assert (u == g["u"]).all()
+    assert err < 1e-4 and err == float(g["err"])
