@@ -3,6 +3,7 @@
 
 #include <cuda_runtime.h>
 
+#include <atomic>
 #include <cstdint>
 #include <cstdio>
 #include <string>
@@ -58,6 +59,27 @@ namespace a3b
 
     // properties of the current device (cached); returns A3B_OK or an error status
     int currentDevice(DeviceProps const** props);
+
+    // device ordinals the library serves (0 .. kMaxDevices-1)
+    constexpr int kMaxDevices = 64;
+
+    // Resident blocks per SM of `kernel` at `threads` threads and no dynamic shared memory, queried once per device
+    // and kept in `cache` (kMaxDevices entries indexed by ordinal, 0 = not queried yet). Threads racing on the first
+    // query store the same value.
+    template<typename Kernel>
+    int residentPerSm(DeviceProps const* props, std::atomic<int>* cache, Kernel kernel, int threads, int* out)
+    {
+        int r = cache[props->ordinal].load(std::memory_order_relaxed);
+        if(r == 0)
+        {
+            int b = 0;
+            A3B_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b, kernel, threads, 0));
+            r = b > 0 ? b : 1;
+            cache[props->ordinal].store(r, std::memory_order_relaxed);
+        }
+        *out = r;
+        return A3B_OK;
+    }
 
     // Bounded-wait limit (ns) passed to kernels that spin.
     uint64_t waitTimeoutNs();

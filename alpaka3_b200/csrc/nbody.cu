@@ -231,14 +231,11 @@ namespace a3b
             int rc = currentDevice(&props);
             if(rc)
                 return rc;
-            static int resident[64] = {0};
-            int& r = resident[props->ordinal];
-            if(r == 0)
-            {
-                int b = 0;
-                A3B_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b, forceKernel, kThreads, 0));
-                r = b > 0 ? b : 1;
-            }
+            static std::atomic<int> resident[kMaxDevices] = {};
+            int r = 0;
+            rc = residentPerSm(props, resident, forceKernel, kThreads, &r);
+            if(rc)
+                return rc;
             unsigned const grid = static_cast<unsigned>(props->smCount) * static_cast<unsigned>(r);
             uint64_t const iBlocks = (iCount + kIBlock - 1) / kIBlock;
             // enough items for ~8 per resident block, slices of at least 2 j-tiles

@@ -468,14 +468,11 @@ namespace a3b
             int rc = currentDevice(&props);
             if(rc)
                 return rc;
-            static int resident[64] = {0};
-            int& r = resident[props->ordinal];
-            if(r == 0)
-            {
-                int b = 0;
-                A3B_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b, reduceAllRanksKernel<T, W, ROp, XOp>, kBlock, 0));
-                r = b > 0 ? b : 1;
-            }
+            static std::atomic<int> resident[kMaxDevices] = {};
+            int r = 0;
+            rc = residentPerSm(props, resident, reduceAllRanksKernel<T, W, ROp, XOp>, kBlock, &r);
+            if(rc)
+                return rc;
             uint64_t const packs = n / W + 1;
             uint64_t const want = (packs + static_cast<uint64_t>(kBlock) * kUnroll - 1) / (kBlock * kUnroll);
             uint64_t const full = static_cast<uint64_t>(props->smCount) * r;
@@ -570,14 +567,11 @@ namespace a3b
             int rc = currentDevice(&props);
             if(rc)
                 return rc;
-            static int resident[64] = {0};
-            int& r = resident[props->ordinal];
-            if(r == 0)
-            {
-                int b = 0;
-                A3B_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b, reduceKernel<T, W, ROp, XOp, PITCHED>, kBlock, 0));
-                r = b > 0 ? b : 1;
-            }
+            static std::atomic<int> resident[kMaxDevices] = {};
+            int r = 0;
+            rc = residentPerSm(props, resident, reduceKernel<T, W, ROp, XOp, PITCHED>, kBlock, &r);
+            if(rc)
+                return rc;
             uint64_t const packs = n / W + 1;
             uint64_t const want = (packs + static_cast<uint64_t>(kBlock) * kUnroll - 1) / (kBlock * kUnroll);
             uint64_t const full = static_cast<uint64_t>(props->smCount) * r;

@@ -21,7 +21,6 @@ namespace a3b
         thread_local std::string tlsError;
         std::atomic<uint64_t> gTimeoutNs{1000000000ull};
 
-        constexpr int kMaxDevices = 64;
         std::mutex gPropsMutex;
         DeviceProps gProps[kMaxDevices];
 

@@ -372,14 +372,11 @@ namespace a3b
         template<typename T, int W, typename Op>
         int gridFor(DeviceProps const* props, uint64_t n, int* grid)
         {
-            static int residentPerSm[64] = {0};
-            int& r = residentPerSm[props->ordinal];
-            if(r == 0)
-            {
-                int b = 0;
-                A3B_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b, streamKernel<T, W, Op>, kBlock, 0));
-                r = b > 0 ? b : 1;
-            }
+            static std::atomic<int> resident[kMaxDevices] = {};
+            int r = 0;
+            int const rc = residentPerSm(props, resident, streamKernel<T, W, Op>, kBlock, &r);
+            if(rc)
+                return rc;
             uint64_t const packs = (n + W - 1) / W;
             uint64_t const want = (packs + static_cast<uint64_t>(kBlock) * kUnroll - 1) / (kBlock * kUnroll);
             uint64_t const full = static_cast<uint64_t>(props->smCount) * r * kWaves;
