@@ -2,8 +2,10 @@
 
 * ``oracle/liboracle.so``     -- the plain-C restatement in ``oracle.c`` (always built).
 * ``oracle/_ref/libalpaka_ref.so`` -- alpaka3's own host backend behind ``ref_harness.cpp``; built only where the
-  reference tree exists (``build_ref.sh``). The built file travels with the repository snapshot; the source tree it
-  is compiled from does not.
+  reference tree exists (``build_ref.sh``).
+* ``oracle/_ref/ref_cuda_bench`` -- alpaka3's own CUDA backend on the benchmark workloads (``ref_cuda_bench.cpp``,
+  nvcc for sm_100a), the reference GPU comparator; built with it.
+The built files travel with the repository snapshot; the source tree they are compiled from does not.
 """
 import os
 import subprocess
@@ -12,6 +14,7 @@ import sys
 HERE = os.path.dirname(os.path.abspath(__file__))
 ORACLE_SO = os.path.join(HERE, "liboracle.so")
 REF_SO = os.path.join(HERE, "_ref", "libalpaka_ref.so")
+REF_CUDA_BENCH = os.path.join(HERE, "_ref", "ref_cuda_bench")
 REFERENCE_ROOT = os.environ.get("ALPAKA_REFERENCE_ROOT", "/root/reference")
 
 
@@ -35,8 +38,8 @@ def build_oracle(force=False):
 def build_ref(force=False):
     if not os.path.isdir(os.path.join(REFERENCE_ROOT, "include", "alpaka")):
         return REF_SO if os.path.exists(REF_SO) else None
-    srcs = [os.path.join(HERE, "ref_harness.cpp"), os.path.join(HERE, "build_ref.sh")]
-    if force or _stale(REF_SO, srcs):
+    srcs = [os.path.join(HERE, f) for f in ("ref_harness.cpp", "ref_ops.hpp", "ref_cuda_bench.cpp", "build_ref.sh")]
+    if force or _stale(REF_SO, srcs) or _stale(REF_CUDA_BENCH, srcs):
         subprocess.check_call(["bash", os.path.join(HERE, "build_ref.sh"), REFERENCE_ROOT])
     return REF_SO
 

@@ -21,3 +21,17 @@ g++ -std=c++20 -O3 -march=x86-64-v3 -fopenmp -ffp-contract=off -fPIC -shared \
     -o "$OUT/libalpaka_ref.so.tmp" "$HERE/ref_harness.cpp"
 mv "$OUT/libalpaka_ref.so.tmp" "$OUT/libalpaka_ref.so"
 echo "built $OUT/libalpaka_ref.so"
+
+# The reference's CUDA backend on the same workloads (GPU comparator), for sm_100a with nvcc's defaults (FMA
+# contraction on, as the reference's own CUDA builds use). Philox inputs come from ../liboracle.so.
+if command -v nvcc > /dev/null && [ -f "$HERE/liboracle.so" ]; then
+    nvcc -x cu -std=c++20 -O3 --expt-relaxed-constexpr --extended-lambda \
+        -gencode arch=compute_100a,code=sm_100a \
+        -I"$REF/include" \
+        -I"$REF/example/heatEquation2D/src" \
+        -I"$REF/example/nBody/src" \
+        -o "$OUT/ref_cuda_bench.tmp" "$HERE/ref_cuda_bench.cpp" \
+        -L"$HERE" -loracle -Xlinker -rpath -Xlinker '$ORIGIN/..'
+    mv "$OUT/ref_cuda_bench.tmp" "$OUT/ref_cuda_bench"
+    echo "built $OUT/ref_cuda_bench"
+fi

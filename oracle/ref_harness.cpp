@@ -30,8 +30,10 @@
 #include "StencilKernel.hpp"   // example/heatEquation2D/src
 #include "analyticalSolution.hpp"
 #include "Kernels.hpp"         // example/nBody/src
+#include "ref_ops.hpp"
 
 using namespace alpaka;
+using namespace a3b_ref;
 
 namespace
 {
@@ -61,91 +63,6 @@ namespace
     {
         return std::chrono::duration<double>(std::chrono::high_resolution_clock::now() - t0).count();
     }
-
-    // ---- BabelStream element-wise operations (babelStreamMainTest.cpp:61-141) ----
-    constexpr double kInitA = 0.1, kInitB = 0.2, kInitC = 0.0, kScalar = 0.4; // babelStreamCommon.hpp:31,45-48
-
-    struct ForEach
-    {
-        ALPAKA_FN_ACC void operator()(
-            auto const& acc,
-            auto const& func,
-            alpaka::concepts::IDataSource auto arg0,
-            alpaka::concepts::IDataSource auto... args) const
-        {
-            onAcc::SimdAlgo{onAcc::worker::threadsInGrid}.concurrent(acc, arg0.getExtents(), func, arg0, args...);
-        }
-    };
-
-    struct InitOp
-    {
-        constexpr void operator()(auto const&, auto a, auto b, auto c) const
-        {
-            using S = ALPAKA_TYPEOF(a.load());
-            a = S::fill(kInitA);
-            b = S::fill(kInitB);
-            c = S::fill(kInitC);
-        }
-    };
-
-    struct CopyOp
-    {
-        constexpr void operator()(auto const&, auto const a, auto c) const
-        {
-            c = a.load();
-        }
-    };
-
-    struct MulOp
-    {
-        constexpr void operator()(auto const&, auto b, auto const c) const
-        {
-            using T = trait::GetValueType_t<ALPAKA_TYPEOF(b)>;
-            b = static_cast<T>(kScalar) * c.load();
-        }
-    };
-
-    struct AddOp
-    {
-        constexpr void operator()(auto const&, auto const a, auto b, auto c) const
-        {
-            c = a.load() + b.load();
-        }
-    };
-
-    struct TriadOp
-    {
-        constexpr void operator()(auto const&, auto a, auto const b, auto const c) const
-        {
-            using T = trait::GetValueType_t<ALPAKA_TYPEOF(a)>;
-            a = b.load() + static_cast<T>(kScalar) * c.load();
-        }
-    };
-
-    struct NStreamOp
-    {
-        constexpr void operator()(auto const&, auto a, auto const b, auto const c) const
-        {
-            using T = trait::GetValueType_t<ALPAKA_TYPEOF(a)>;
-            a = a.load() + b.load() + static_cast<T>(kScalar) * c.load();
-        }
-    };
-
-    struct Product
-    {
-        constexpr auto operator()(auto&& x, auto&& y) const
-        {
-            return x * y;
-        }
-    };
-
-    struct Square
-    {
-        constexpr auto operator()(auto&& x) const
-        {
-            return x * x;
-        }
-    };
 
     // min/max reduce functors as the reference test declares them (test/unit/algorithm/reduce.cpp:22-56)
     struct MinValue
