@@ -4,15 +4,20 @@
 // and SimdTransformReduce::reduceSimdPackExecution (include/alpaka/onAcc/internal/SimdTransformReduce.hpp:359-499).
 //
 // Design (one launch, no pre-fill of `out`):
-//   * a resident grid (SM count x resident blocks) walks the input in 16-byte packs, UNROLL packs per thread per
-//     iteration, each into its own accumulator (independent dependency chains);
+//   * the input is cut into chunks of 256 threads x ppt packs (ppt = 8 packs of 32 bytes, i.e. 64 KB, for large
+//     inputs; fewer for small ones so that there are still ~2048 chunks) and block b reduces chunk b: a full grid of
+//     short-lived blocks that the scheduler hands out in index order, so the GPU sweeps the input front to back. On
+//     B200 this read 7.48 TB/s against 7.17-7.20 TB/s for a resident grid walking the input grid-stride;
+//   * each thread keeps ppt independent accumulators (all its loads of a chunk are in flight together);
 //   * fp32 inputs: the transformed elements of one pack are summed in fp32, the pack sum is added to an fp64
 //     accumulator; fp64 inputs accumulate in fp64; integer + accumulates in 64-bit unsigned (wraps like the
 //     reference's atomicAdd on the narrow type once truncated);
 //   * warp butterfly (shfl_xor), then a block step through shared memory, gives one partial per block;
-//   * the last block to finish (threadfence + atomic ticket) combines the partials in block order and writes out[0],
-//     then resets the ticket, so the scratch is left ready for the next call on the stream.
-// The result depends only on (device SM count, n): repeated runs give identical bits.
+//   * two-level last-block-done: the last block of each group of 256 blocks (threadfence + atomic ticket) combines
+//     the group's partials, one per thread, into a group partial; the last group combines the group partials and
+//     writes out[0]. Every ticket is reset by the block that drew the last number, so the scratch is left ready for
+//     the next call on the stream.
+// The combination order depends only on n: repeated runs, and runs on GPUs with other SM counts, give identical bits.
 #include <cfloat>
 #include <climits>
 #include <mutex>
@@ -25,8 +30,38 @@ namespace a3b
     namespace
     {
         constexpr int kBlock = 256;
-        constexpr int kUnroll = 4;
         constexpr int kWarps = kBlock / 32;
+        constexpr int kMaxPpt = 8;                 // packs per thread per chunk, at most (16-byte packs)
+        constexpr unsigned kGroup = kBlock;        // blocks per first-level group: one partial per thread
+        constexpr uint64_t kMaxGrid = 1ull << 20;  // blocks; larger inputs (and capped grids) loop over chunks
+        constexpr uint64_t kTargetChunks = 2048;   // smaller inputs get smaller chunks, down to ppt = 1
+        constexpr unsigned kMaxGroups = static_cast<unsigned>(kMaxGrid / kGroup);
+
+        // Packs per thread per chunk, at most: 128 bytes in flight per thread over all inputs (Σx²: 4 packs of 32
+        // bytes; dot: 2 of each input), at most kMaxPpt; this keeps the kernels at 64 registers or fewer, 4 resident
+        // blocks per SM.
+        template<typename T, int W, int XOp>
+        __host__ __device__ constexpr int maxPpt()
+        {
+            constexpr int bytes = W * static_cast<int>(sizeof(T)) * (XOp == A3B_XFORM_PRODUCT ? 2 : 1);
+            return bytes >= 128 ? 1 : (128 / bytes < kMaxPpt ? 128 / bytes : kMaxPpt);
+        }
+
+        // Packs per thread per chunk for nPacks packs: the largest of maxPpt, ..., 2, 1 that still leaves
+        // kTargetChunks chunks (a function of n alone, so the combination order does not depend on the device).
+        inline int pptFor(uint64_t nPacks, int maxPpt)
+        {
+            int ppt = maxPpt;
+            while(ppt > 1 && nPacks < kTargetChunks * kBlock * static_cast<uint64_t>(ppt))
+                ppt /= 2;
+            return ppt;
+        }
+
+        inline uint64_t chunksFor(uint64_t nPacks, int ppt)
+        {
+            uint64_t const chunk = static_cast<uint64_t>(kBlock) * static_cast<uint64_t>(ppt);
+            return (nPacks + chunk - 1) / chunk;
+        }
 
         // accumulator type
         template<typename T, int ROp>
@@ -183,11 +218,44 @@ namespace a3b
             return r;
         }
 
-        struct ReduceScratch
+        // Scratch of one reduction: the final ticket, one ticket and one partial per group, one partial per block.
+        // Tickets start at zero (fresh scratch is zero-filled) and are reset by the block that drew the last number.
+        template<typename A>
+        struct ReduceWork
         {
-            unsigned ticket;
-            unsigned pad[15];
+            unsigned* ticket;
+            unsigned* groupTickets;
+            A* groupPartials;
+            A* partials;
         };
+
+        inline size_t roundUp64(size_t b)
+        {
+            return (b + 63u) & ~size_t{63u};
+        }
+
+        // bytes of scratch for `grid` blocks with room for `maxGroups` groups
+        template<typename A>
+        size_t workBytes(unsigned maxGroups, uint64_t grid)
+        {
+            return 64u + roundUp64(sizeof(unsigned) * maxGroups) + roundUp64(sizeof(A) * maxGroups)
+                   + sizeof(A) * static_cast<size_t>(grid);
+        }
+
+        // the layout at `base`: the tickets first (a caller that must clear them clears the first
+        // 64 + roundUp64(4 * maxGroups) bytes), the partials after them
+        template<typename A>
+        ReduceWork<A> workAt(void* base, unsigned maxGroups)
+        {
+            auto* b = static_cast<unsigned char*>(base);
+            ReduceWork<A> w;
+            w.ticket = reinterpret_cast<unsigned*>(b);
+            w.groupTickets = reinterpret_cast<unsigned*>(b + 64);
+            size_t const off = 64u + roundUp64(sizeof(unsigned) * maxGroups);
+            w.groupPartials = reinterpret_cast<A*>(b + off);
+            w.partials = reinterpret_cast<A*>(b + off + roundUp64(sizeof(A) * maxGroups));
+            return w;
+        }
 
         // Finish: convert accumulator to the output element (or store the raw partial).
         template<typename T, typename A>
@@ -212,9 +280,12 @@ namespace a3b
             }
         }
 
-        // This block's partial (identical in every thread on return). PITCHED: rows of rowLen elements, rowPitch bytes
-        // apart; packs never straddle rows (rowLen % W == 0).
-        template<typename T, int W, int ROp, int XOp, bool PITCHED>
+        // This block's partial (identical in every thread on return). Without LOOP the grid has one block per chunk
+        // and block b reduces chunk b; with LOOP (grids capped below the chunk count) block b takes chunks b,
+        // b + gridDim.x, ... A full chunk at ppt == U loads all its packs at once (compile-time count, no
+        // predicates: the fewest registers); other chunks go pack by pack. PITCHED: rows of rowLen elements,
+        // rowPitch bytes apart; packs never straddle rows (rowLen % W == 0).
+        template<typename T, int W, int ROp, int XOp, bool PITCHED, bool LOOP>
         __device__ __forceinline__ typename AccOf<T, ROp>::type blockPartial(
             T const* __restrict__ in0,
             T const* __restrict__ in1,
@@ -222,13 +293,15 @@ namespace a3b
             uint64_t rowLen,
             uint64_t rowPitch,
             T neutral,
+            int ppt,
             typename AccOf<T, ROp>::type* smem)
         {
             using A = typename AccOf<T, ROp>::type;
+            constexpr int U = maxPpt<T, W, XOp>();
             A const neutralA = widen<A>(neutral);
-            A acc[kUnroll];
+            A acc[U];
 #pragma unroll
-            for(int u = 0; u < kUnroll; ++u)
+            for(int u = 0; u < U; ++u)
                 acc[u] = neutralA;
 
             uint64_t const nPacks = n / W;
@@ -245,37 +318,52 @@ namespace a3b
                     return base + p * W;
             };
 
-            uint64_t const S = static_cast<uint64_t>(gridDim.x) * kBlock;
-            uint64_t i = static_cast<uint64_t>(blockIdx.x) * kBlock + threadIdx.x;
-            for(; i + (kUnroll - 1) * S < nPacks; i += kUnroll * S)
+            uint64_t const chunk = static_cast<uint64_t>(kBlock) * static_cast<uint64_t>(ppt);
+            uint64_t const nChunks = (nPacks + chunk - 1) / chunk;
+            auto reduceChunk = [&](uint64_t c)
             {
-                Pack<T, W> x[kUnroll], y[kUnroll];
-#pragma unroll
-                for(int u = 0; u < kUnroll; ++u)
+                uint64_t const first = c * chunk + threadIdx.x;
+                if(ppt == U && c * chunk + chunk <= nPacks)
                 {
-                    x[u] = loadPack<T, W>(addr(in0, i + u * S), 0);
-                    if constexpr(XOp == A3B_XFORM_PRODUCT)
-                        y[u] = loadPack<T, W>(addr(in1, i + u * S), 0);
-                    else
-                        y[u] = x[u];
+                    Pack<T, W> x[U], y[U];
+#pragma unroll
+                    for(int u = 0; u < U; ++u)
+                    {
+                        uint64_t const p = first + static_cast<uint64_t>(u) * kBlock;
+                        x[u] = loadPack<T, W>(addr(in0, p), 0);
+                        if constexpr(XOp == A3B_XFORM_PRODUCT)
+                            y[u] = loadPack<T, W>(addr(in1, p), 0);
+                        else
+                            y[u] = x[u];
+                    }
+#pragma unroll
+                    for(int u = 0; u < U; ++u)
+                        acc[u] = foldPack<T, W, ROp, XOp>(acc[u], x[u], y[u]);
                 }
+                else
+                {
 #pragma unroll
-                for(int u = 0; u < kUnroll; ++u)
-                    acc[u] = foldPack<T, W, ROp, XOp>(acc[u], x[u], y[u]);
-            }
-#pragma unroll
-            for(int u = 0; u < kUnroll; ++u)
+                    for(int u = 0; u < U; ++u)
+                    {
+                        uint64_t const p = first + static_cast<uint64_t>(u) * kBlock;
+                        if(u < ppt && p < nPacks)
+                        {
+                            Pack<T, W> x = loadPack<T, W>(addr(in0, p), 0);
+                            Pack<T, W> y = x;
+                            if constexpr(XOp == A3B_XFORM_PRODUCT)
+                                y = loadPack<T, W>(addr(in1, p), 0);
+                            acc[u] = foldPack<T, W, ROp, XOp>(acc[u], x, y);
+                        }
+                    }
+                }
+            };
+            if constexpr(LOOP)
             {
-                uint64_t const p = i + u * S;
-                if(p < nPacks)
-                {
-                    Pack<T, W> x = loadPack<T, W>(addr(in0, p), 0);
-                    Pack<T, W> y = x;
-                    if constexpr(XOp == A3B_XFORM_PRODUCT)
-                        y = loadPack<T, W>(addr(in1, p), 0);
-                    acc[u] = foldPack<T, W, ROp, XOp>(acc[u], x, y);
-                }
+                for(uint64_t c = blockIdx.x; c < nChunks; c += gridDim.x)
+                    reduceChunk(c);
             }
+            else if(blockIdx.x < nChunks)
+                reduceChunk(blockIdx.x);
             if constexpr(W > 1 && !PITCHED)
             {
                 uint64_t const e = nPacks * W + static_cast<uint64_t>(blockIdx.x) * kBlock + threadIdx.x;
@@ -291,13 +379,62 @@ namespace a3b
 
             A v = acc[0];
 #pragma unroll
-            for(int u = 1; u < kUnroll; ++u)
+            for(int u = 1; u < U; ++u)
                 v = combine<A, ROp>(v, acc[u]);
             v = blockReduce<A, ROp>(v, smem);
             return v;
         }
 
-        template<typename T, int W, int ROp, int XOp, bool PITCHED>
+        // Two-level last-block-done combination of the block partials `v` (identical in every thread). Returns true
+        // in every thread of the one block that finishes last, with the grid's total in *total; false elsewhere.
+        template<typename A, int ROp>
+        __device__ __forceinline__ bool combineGrid(A v, A neutralA, ReduceWork<A> const& w, A* smem, bool* flag, A* total)
+        {
+            unsigned const g = blockIdx.x / kGroup;
+            unsigned const nGroups = (gridDim.x + kGroup - 1) / kGroup;
+            unsigned const inGroup = min(kGroup, gridDim.x - g * kGroup);
+            if(threadIdx.x == 0)
+            {
+                w.partials[blockIdx.x] = v;
+                __threadfence();
+                *flag = atomicAdd(w.groupTickets + g, 1u) == inGroup - 1u;
+            }
+            __syncthreads();
+            if(!*flag)
+                return false;
+            __threadfence();
+            // the group's partials, one per thread, in block order
+            A r = threadIdx.x < inGroup ? __ldcg(w.partials + g * kGroup + threadIdx.x) : neutralA;
+            r = blockReduce<A, ROp>(r, smem); // its barriers order every thread's read of *flag before the next write
+            if(nGroups == 1u)
+            {
+                if(threadIdx.x == 0)
+                    w.groupTickets[g] = 0u;
+                *total = r;
+                return true;
+            }
+            if(threadIdx.x == 0)
+            {
+                w.groupTickets[g] = 0u;
+                w.groupPartials[g] = r;
+                __threadfence();
+                *flag = atomicAdd(w.ticket, 1u) == nGroups - 1u;
+            }
+            __syncthreads();
+            if(!*flag)
+                return false;
+            __threadfence();
+            A t = neutralA;
+            for(unsigned k = threadIdx.x; k < nGroups; k += kBlock)
+                t = combine<A, ROp>(t, __ldcg(w.groupPartials + k));
+            t = blockReduce<A, ROp>(t, smem);
+            if(threadIdx.x == 0)
+                *w.ticket = 0u;
+            *total = t;
+            return true;
+        }
+
+        template<typename T, int W, int ROp, int XOp, bool PITCHED, bool LOOP>
         __global__ void __launch_bounds__(kBlock) reduceKernel(
             T const* __restrict__ in0,
             T const* __restrict__ in1,
@@ -305,38 +442,20 @@ namespace a3b
             uint64_t rowLen,
             uint64_t rowPitch,
             T neutral,
+            int ppt,
             void* out,
             bool rawPartial,
-            ReduceScratch* scratch,
-            typename AccOf<T, ROp>::type* partials)
+            ReduceWork<typename AccOf<T, ROp>::type> work)
         {
             using A = typename AccOf<T, ROp>::type;
             __shared__ A smem[kWarps];
-            __shared__ bool amLast;
-            A const neutralA = widen<A>(neutral);
-            A const v = blockPartial<T, W, ROp, XOp, PITCHED>(in0, in1, n, rowLen, rowPitch, neutral, smem);
-
-            if(threadIdx.x == 0)
-            {
-                partials[blockIdx.x] = v;
-                __threadfence();
-                unsigned const t = atomicAdd(&scratch->ticket, 1u);
-                amLast = (t == gridDim.x - 1u);
-            }
-            __syncthreads();
-            if(!amLast)
+            __shared__ bool flag;
+            A const v = blockPartial<T, W, ROp, XOp, PITCHED, LOOP>(in0, in1, n, rowLen, rowPitch, neutral, ppt, smem);
+            A total;
+            if(!combineGrid<A, ROp>(v, widen<A>(neutral), work, smem, &flag, &total))
                 return;
-            __threadfence();
-            // last block: combine all partials in block order (fixed tree => deterministic)
-            A r = neutralA;
-            for(unsigned b = threadIdx.x; b < gridDim.x; b += kBlock)
-                r = combine<A, ROp>(r, __ldcg(partials + b));
-            r = blockReduce<A, ROp>(r, smem);
             if(threadIdx.x == 0)
-            {
-                writeResult<T, A>(out, r, rawPartial);
-                scratch->ticket = 0u; // ready for the next call on this stream
-            }
+                writeResult<T, A>(out, total, rawPartial);
         }
 
         // ---------------------------------------------------------------- fused with the all-reduce over peers
@@ -369,15 +488,15 @@ namespace a3b
         // the world's values in its own buffer and combines them in rank order: every rank computes the same bits.
         // With lowerRanksOnly the combination covers ranks 0 .. rank-1 (the carry of a scan split across ranks); the
         // wait still covers every rank, so one call's slots are never overwritten by the next call too early.
-        template<typename T, int W, int ROp, int XOp>
+        template<typename T, int W, int ROp, int XOp, bool LOOP>
         __global__ void __launch_bounds__(kBlock) reduceAllRanksKernel(
             T const* __restrict__ in0,
             T const* __restrict__ in1,
             uint64_t n,
             T neutral,
+            int ppt,
             void* out,
-            ReduceScratch* scratch,
-            typename AccOf<T, ROp>::type* partials,
+            ReduceWork<typename AccOf<T, ROp>::type> work,
             PeerSlots peers,
             bool lowerRanksOnly,
             unsigned* errWord,
@@ -385,30 +504,16 @@ namespace a3b
         {
             using A = typename AccOf<T, ROp>::type;
             __shared__ A smem[kWarps];
-            __shared__ bool amLast;
+            __shared__ bool flag;
             A const neutralA = widen<A>(neutral);
-            A const v = blockPartial<T, W, ROp, XOp, false>(in0, in1, n, n, 0, neutral, smem);
-            if(threadIdx.x == 0)
-            {
-                partials[blockIdx.x] = v;
-                __threadfence();
-                unsigned const t = atomicAdd(&scratch->ticket, 1u);
-                amLast = (t == gridDim.x - 1u);
-            }
-            __syncthreads();
-            if(!amLast)
+            A const v = blockPartial<T, W, ROp, XOp, false, LOOP>(in0, in1, n, n, 0, neutral, ppt, smem);
+            A r;
+            if(!combineGrid<A, ROp>(v, neutralA, work, smem, &flag, &r))
                 return;
-            __threadfence();
-            A r = neutralA;
-            for(unsigned b = threadIdx.x; b < gridDim.x; b += kBlock)
-                r = combine<A, ROp>(r, __ldcg(partials + b));
-            r = blockReduce<A, ROp>(r, smem);
             if(threadIdx.x >= 32)
                 return;
             // warp 0: lane q exchanges with rank q (all ranks in parallel, one system-scope fence per lane)
             int const lane = threadIdx.x;
-            if(lane == 0)
-                scratch->ticket = 0u;
             static_assert(sizeof(A) <= 8, "partials are exchanged as 8-byte words");
             unsigned long long bits = 0;
             memcpy(&bits, &r, sizeof(A));
@@ -468,27 +573,25 @@ namespace a3b
             int rc = currentDevice(&props);
             if(rc)
                 return rc;
-            static std::atomic<int> resident[kMaxDevices] = {};
-            int r = 0;
-            rc = residentPerSm(props, resident, reduceAllRanksKernel<T, W, ROp, XOp>, kBlock, &r);
-            if(rc)
-                return rc;
-            uint64_t const packs = n / W + 1;
-            uint64_t const want = (packs + static_cast<uint64_t>(kBlock) * kUnroll - 1) / (kBlock * kUnroll);
-            uint64_t const full = static_cast<uint64_t>(props->smCount) * r;
-            int const grid = static_cast<int>(want < full ? (want > 0 ? want : 1) : full);
+            int const ppt = pptFor(n / W, maxPpt<T, W, XOp>());
+            uint64_t const chunks = chunksFor(n / W, ppt);
+            bool const loop = chunks > kMaxGrid;
+            uint64_t const grid = loop ? kMaxGrid : (chunks > 0 ? chunks : 1);
             void* scr = nullptr;
-            rc = streamScratch(s, kScratchReduce, sizeof(ReduceScratch) + sizeof(A) * static_cast<size_t>(full), &scr);
+            rc = streamScratch(s, kScratchReduce, workBytes<A>(kMaxGroups, grid), &scr);
             if(rc)
                 return rc;
             PeerSlots peers;
             rc = peerSlots(g, &peers);
             if(rc)
                 return rc;
-            auto* hdr = static_cast<ReduceScratch*>(scr);
-            reduceAllRanksKernel<T, W, ROp, XOp><<<grid, kBlock, 0, s>>>(
-                in0, in1, n, neutral, out, hdr, reinterpret_cast<A*>(hdr + 1), peers, lower, props->errWord,
-                waitTimeoutNs());
+            auto const w = workAt<A>(scr, kMaxGroups);
+            if(loop)
+                reduceAllRanksKernel<T, W, ROp, XOp, true><<<static_cast<unsigned>(grid), kBlock, 0, s>>>(
+                    in0, in1, n, neutral, ppt, out, w, peers, lower, props->errWord, waitTimeoutNs());
+            else
+                reduceAllRanksKernel<T, W, ROp, XOp, false><<<static_cast<unsigned>(grid), kBlock, 0, s>>>(
+                    in0, in1, n, neutral, ppt, out, w, peers, lower, props->errWord, waitTimeoutNs());
             A3B_CHECK_LAUNCH("transform_reduce_allranks launch");
             return A3B_OK;
         }
@@ -567,24 +670,21 @@ namespace a3b
             int rc = currentDevice(&props);
             if(rc)
                 return rc;
-            static std::atomic<int> resident[kMaxDevices] = {};
-            int r = 0;
-            rc = residentPerSm(props, resident, reduceKernel<T, W, ROp, XOp, PITCHED>, kBlock, &r);
-            if(rc)
-                return rc;
-            uint64_t const packs = n / W + 1;
-            uint64_t const want = (packs + static_cast<uint64_t>(kBlock) * kUnroll - 1) / (kBlock * kUnroll);
-            uint64_t const full = static_cast<uint64_t>(props->smCount) * r;
-            int const grid = static_cast<int>(want < full ? (want > 0 ? want : 1) : full);
-
+            int const ppt = pptFor(n / W, maxPpt<T, W, XOp>());
+            uint64_t const chunks = chunksFor(n / W, ppt);
+            bool const loop = chunks > kMaxGrid;
+            uint64_t const grid = loop ? kMaxGrid : (chunks > 0 ? chunks : 1);
             void* scr = nullptr;
-            rc = streamScratch(s, kScratchReduce, sizeof(ReduceScratch) + sizeof(A) * static_cast<size_t>(full), &scr);
+            rc = streamScratch(s, kScratchReduce, workBytes<A>(kMaxGroups, grid), &scr);
             if(rc)
                 return rc;
-            auto* hdr = static_cast<ReduceScratch*>(scr);
-            auto* partials = reinterpret_cast<A*>(hdr + 1);
-            reduceKernel<T, W, ROp, XOp, PITCHED>
-                <<<grid, kBlock, 0, s>>>(in0, in1, n, rowLen, rowPitch, neutral, out, raw, hdr, partials);
+            auto const w = workAt<A>(scr, kMaxGroups);
+            if(loop)
+                reduceKernel<T, W, ROp, XOp, PITCHED, true><<<static_cast<unsigned>(grid), kBlock, 0, s>>>(
+                    in0, in1, n, rowLen, rowPitch, neutral, ppt, out, raw, w);
+            else
+                reduceKernel<T, W, ROp, XOp, PITCHED, false><<<static_cast<unsigned>(grid), kBlock, 0, s>>>(
+                    in0, in1, n, rowLen, rowPitch, neutral, ppt, out, raw, w);
             A3B_CHECK_LAUNCH("transform_reduce launch");
             return A3B_OK;
         }
@@ -733,7 +833,8 @@ namespace a3b
         // accounted memory footprint, and latency-critical loops that cannot afford an allocation's implicit
         // synchronisation. Its scratch (ticket header + one 8-byte partial per block) lives in this fixed static
         // array, which every device that loads the library holds until the process exits.
-        constexpr size_t kNoAllocScratchBytes = 16384; // 64-byte header + up to 2040 block partials
+        constexpr size_t kNoAllocScratchBytes = 16384; // tickets for 8 groups + 8 group partials + 2024 partials
+        constexpr unsigned kNoAllocGroups = 8;
         __device__ __align__(256) unsigned char g_noAllocScratch[kNoAllocScratchBytes];
 
         std::mutex gNoAllocMutex;
@@ -768,17 +869,18 @@ namespace a3b
             int rc = currentDevice(&props);
             if(rc)
                 return rc;
-            int b = 0;
-            A3B_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b, reduceKernel<T, W, ROp, XOp, false>, kBlock, 0));
-            uint64_t const packs = n / W + 1;
-            uint64_t const want = (packs + static_cast<uint64_t>(kBlock) * kUnroll - 1) / (kBlock * kUnroll);
-            uint64_t const full = static_cast<uint64_t>(props->smCount) * static_cast<uint64_t>(b > 0 ? b : 1);
-            uint64_t const grid = want < full ? (want > 0 ? want : 1) : full;
-            size_t const need = sizeof(ReduceScratch) + sizeof(A) * static_cast<size_t>(grid);
+            // as many blocks as the array has room for partials; larger inputs give each block several chunks
+            size_t const fixed = workBytes<A>(kNoAllocGroups, 0);
+            uint64_t const room = (kNoAllocScratchBytes - fixed) / sizeof(A);
+            uint64_t const cap = room < uint64_t{kNoAllocGroups} * kGroup ? room : uint64_t{kNoAllocGroups} * kGroup;
+            int const ppt = pptFor(n / W, maxPpt<T, W, XOp>());
+            uint64_t const chunks = chunksFor(n / W, ppt);
+            uint64_t const grid = chunks < cap ? (chunks > 0 ? chunks : 1) : cap;
+            size_t const need = workBytes<A>(kNoAllocGroups, grid);
             if(need > kNoAllocScratchBytes)
             {
-                setError("a3b_transform_reduce_noalloc needs %zu bytes of scratch for %llu blocks on this device, "
-                         "more than its fixed %zu-byte static array",
+                setError("a3b_transform_reduce_noalloc needs %zu bytes of scratch for %llu blocks, more than its fixed "
+                         "%zu-byte static array",
                          need, static_cast<unsigned long long>(grid), kNoAllocScratchBytes);
                 return A3B_ERR_TOO_LARGE;
             }
@@ -786,12 +888,10 @@ namespace a3b
             rc = noAllocScratch(&scr);
             if(rc)
                 return rc;
-            auto* hdr = static_cast<ReduceScratch*>(scr);
-            // the array keeps the previous call's contents: the block ticket must start at zero
-            A3B_CUDA(cudaMemsetAsync(hdr, 0, sizeof(ReduceScratch), s));
-            auto* partials = reinterpret_cast<A*>(hdr + 1);
-            reduceKernel<T, W, ROp, XOp, false><<<static_cast<unsigned>(grid), kBlock, 0, s>>>(
-                in0, in1, n, n, 0, neutral, out, false, hdr, partials);
+            // the array keeps the previous call's contents: the tickets must start at zero
+            A3B_CUDA(cudaMemsetAsync(scr, 0, 64u + roundUp64(sizeof(unsigned) * kNoAllocGroups), s));
+            reduceKernel<T, W, ROp, XOp, false, true><<<static_cast<unsigned>(grid), kBlock, 0, s>>>(
+                in0, in1, n, n, 0, neutral, ppt, out, false, workAt<A>(scr, kNoAllocGroups));
             A3B_CHECK_LAUNCH("transform_reduce_noalloc launch");
             return A3B_OK;
         }

@@ -6,11 +6,12 @@
 // SimdIotaKernel / generic fill (include/alpaka/onHost/algo/internal/transform.hpp:21-107, concurrent.hpp:18-67,
 // iota.hpp:19-75, include/alpaka/api/generic.hpp:45-88).
 //
-// Design: every array is walked in 32-byte packs (one 256-bit load/store instruction each on sm_100; 16-byte packs
-// when a pointer is only 16-byte aligned, single elements otherwise); a thread handles UNROLL packs per iteration at
-// indices i, i + S, i + 2S, ... (S = threads in the grid), so each load/store instruction of a warp covers 1 KB of
-// contiguous memory and UNROLL independent loads per array are in flight per thread. The grid is two waves of
-// (SM count x resident blocks), which measured best on B200 for 2^25..2^28-element arrays.
+// Design: the arrays are cut into chunks of 256 threads x 32 bytes per array (one 256-bit load/store instruction per
+// thread on sm_100 when every pointer is 32-byte aligned; two 16-byte packs when 16-byte aligned; single elements
+// otherwise), and block b handles chunk b: a full grid of short-lived blocks, which the block scheduler hands out in
+// index order, so the whole GPU sweeps memory front to back. On B200 this measured 5-7% faster than a resident grid
+// walking the arrays grid-stride (copy 6.55 vs 6.24 TB/s, triad 6.84 vs 6.50 TB/s on 2^25 fp64 arrays). Beyond 2^31
+// chunks (2^39 packs) the call is rejected.
 // Floating-point operations use explicitly rounded intrinsics, so results are bit-identical to an IEEE CPU
 // evaluation of the same expression without contraction.
 #include <type_traits>
@@ -21,15 +22,16 @@ namespace a3b
 {
     namespace
     {
-#ifndef A3B_STREAM_UNROLL
-#define A3B_STREAM_UNROLL 2
-#endif
-#ifndef A3B_STREAM_WAVES
-#define A3B_STREAM_WAVES 2
-#endif
         constexpr int kBlock = 256;
-        constexpr int kUnroll = A3B_STREAM_UNROLL; // packs per array per thread per iteration
-        constexpr int kWaves = A3B_STREAM_WAVES;   // grid = kWaves x (SMs x resident blocks)
+        constexpr uint64_t kMaxGrid = 1ull << 31; // gridDim.x limit
+
+        // packs per thread per chunk: 32 bytes of each array
+        template<typename T, int W>
+        __host__ __device__ constexpr int packsPerThread()
+        {
+            constexpr int bytes = W * static_cast<int>(sizeof(T));
+            return bytes >= 32 ? 1 : 32 / bytes;
+        }
 
         template<typename T, int W>
         struct alignas(W * sizeof(T) >= 32 ? 32 : 16) Pack
@@ -274,18 +276,18 @@ namespace a3b
             }
         };
 
-        template<typename T, int W, typename Op>
+        template<typename T, int W, int U, typename Op>
         __device__ __forceinline__ void applyPacks(
             Op const& op,
             T* p0,
             T* p1,
             T* p2,
-            uint64_t const (&idx)[kUnroll],
+            uint64_t const (&idx)[U],
             int count)
         {
-            Pack<T, W> a[kUnroll], b[kUnroll], c[kUnroll];
+            Pack<T, W> a[U], b[U], c[U];
 #pragma unroll
-            for(int u = 0; u < kUnroll; ++u)
+            for(int u = 0; u < U; ++u)
             {
                 if(u < count)
                 {
@@ -298,7 +300,7 @@ namespace a3b
                 }
             }
 #pragma unroll
-            for(int u = 0; u < kUnroll; ++u)
+            for(int u = 0; u < U; ++u)
             {
                 if(u < count)
                 {
@@ -315,34 +317,32 @@ namespace a3b
             }
         }
 
-        // W elements per pack (16 bytes when all pointers are 16-byte aligned, else 1)
+        // W elements per pack; block c covers packs [c * kBlock * U, (c + 1) * kBlock * U), thread t takes packs
+        // c * kBlock * U + u * kBlock + t (each warp instruction covers 32 consecutive packs). The grid has one block
+        // per chunk (at least one): a full chunk moves all its packs at once with no predicates, the last chunk
+        // checks each pack.
         template<typename T, int W, typename Op>
         __global__ void __launch_bounds__(kBlock) streamKernel(Op op, T* p0, T* p1, T* p2, uint64_t n)
         {
+            constexpr int U = packsPerThread<T, W>();
             uint64_t const nPacks = n / W;
-            uint64_t const S = static_cast<uint64_t>(gridDim.x) * kBlock;
-            uint64_t i = static_cast<uint64_t>(blockIdx.x) * kBlock + threadIdx.x;
-            for(; i + (kUnroll - 1) * S < nPacks; i += kUnroll * S)
-            {
-                uint64_t idx[kUnroll];
+            uint64_t const chunk = static_cast<uint64_t>(kBlock) * U;
+            uint64_t const c = blockIdx.x;
+            uint64_t idx[U];
 #pragma unroll
-                for(int u = 0; u < kUnroll; ++u)
-                    idx[u] = i + u * S;
-                applyPacks<T, W>(op, p0, p1, p2, idx, kUnroll);
-            }
+            for(int u = 0; u < U; ++u)
+                idx[u] = c * chunk + static_cast<uint64_t>(u) * kBlock + threadIdx.x;
+            if(c * chunk + chunk <= nPacks)
+                applyPacks<T, W, U>(op, p0, p1, p2, idx, U);
+            else
             {
-                // remaining packs: fewer than kUnroll per thread
-                uint64_t idx[kUnroll];
                 int count = 0;
 #pragma unroll
-                for(int u = 0; u < kUnroll; ++u)
-                {
-                    idx[u] = i + u * S;
+                for(int u = 0; u < U; ++u)
                     if(idx[u] < nPacks)
                         count = u + 1;
-                }
                 if(count > 0)
-                    applyPacks<T, W>(op, p0, p1, p2, idx, count);
+                    applyPacks<T, W, U>(op, p0, p1, p2, idx, count);
             }
             if constexpr(W > 1)
             {
@@ -369,20 +369,16 @@ namespace a3b
             }
         }
 
-        template<typename T, int W, typename Op>
-        int gridFor(DeviceProps const* props, uint64_t n, int* grid)
+        // one block per chunk (at least one, so the tail elements of a pack-less array are handled); 0 when the
+        // array needs more blocks than a grid holds (more than 2^39 packs)
+        template<typename T, int W>
+        unsigned gridFor(uint64_t n)
         {
-            static std::atomic<int> resident[kMaxDevices] = {};
-            int r = 0;
-            int const rc = residentPerSm(props, resident, streamKernel<T, W, Op>, kBlock, &r);
-            if(rc)
-                return rc;
-            uint64_t const packs = (n + W - 1) / W;
-            uint64_t const want = (packs + static_cast<uint64_t>(kBlock) * kUnroll - 1) / (kBlock * kUnroll);
-            uint64_t const full = static_cast<uint64_t>(props->smCount) * r * kWaves;
-            uint64_t g = want < full ? want : full;
-            *grid = static_cast<int>(g > 0 ? g : 1);
-            return A3B_OK;
+            uint64_t const chunk = static_cast<uint64_t>(kBlock) * packsPerThread<T, W>();
+            uint64_t const chunks = (n / W + chunk - 1) / chunk;
+            if(chunks >= kMaxGrid)
+                return 0u;
+            return static_cast<unsigned>(chunks > 0 ? chunks : 1);
         }
 
         template<typename T, typename Op>
@@ -400,30 +396,20 @@ namespace a3b
                 return (!(Op::R & 1 || Op::Wr & 1) || ok(p0)) && (!(Op::R & 2 || Op::Wr & 2) || ok(p1))
                        && (!(Op::R & 4 || Op::Wr & 4) || ok(p2));
             };
-            int grid = 1;
-            if(alignedTo(32))
+            constexpr int W32 = 32 / sizeof(T), W16 = packWidth<T>();
+            bool const a32 = alignedTo(32), a16 = alignedTo(16);
+            unsigned const grid = a32 ? gridFor<T, W32>(n) : a16 ? gridFor<T, W16>(n) : gridFor<T, 1>(n);
+            if(grid == 0u)
             {
-                constexpr int W = 32 / sizeof(T);
-                rc = gridFor<T, W, Op>(props, n, &grid);
-                if(rc)
-                    return rc;
-                streamKernel<T, W, Op><<<grid, kBlock, 0, s>>>(op, p0, p1, p2, n);
+                setError("array of %llu elements needs more blocks than a grid holds", static_cast<unsigned long long>(n));
+                return A3B_ERR_TOO_LARGE;
             }
-            else if(alignedTo(16))
-            {
-                constexpr int W = packWidth<T>();
-                rc = gridFor<T, W, Op>(props, n, &grid);
-                if(rc)
-                    return rc;
-                streamKernel<T, W, Op><<<grid, kBlock, 0, s>>>(op, p0, p1, p2, n);
-            }
+            if(a32)
+                streamKernel<T, W32, Op><<<grid, kBlock, 0, s>>>(op, p0, p1, p2, n);
+            else if(a16)
+                streamKernel<T, W16, Op><<<grid, kBlock, 0, s>>>(op, p0, p1, p2, n);
             else
-            {
-                rc = gridFor<T, 1, Op>(props, n, &grid);
-                if(rc)
-                    return rc;
                 streamKernel<T, 1, Op><<<grid, kBlock, 0, s>>>(op, p0, p1, p2, n);
-            }
             A3B_CHECK_LAUNCH("stream kernel launch");
             return A3B_OK;
         }

@@ -8,8 +8,8 @@
  *
  * Each workload calls the reference the way its own benchmark or example does:
  *   sumsq      onHost::transformReduce(q, gpuCuda, 0.f, out, std::plus, square, in)   (onHost/algo/transformReduce.hpp:59-114)
- *   babelstream SimdAlgo::concurrent kernels enqueued with the benchmark's FrameSpec     (babelStreamMainTest.cpp:224-227,
- *              285-366); dot through onHost::transformReduce                            (:337-345)
+ *   babelstream SimdAlgo::concurrent kernels enqueued with the benchmark's FrameSpec     (babelStreamMainTest.cpp:224-227),
+ *              each operation timed on its own; dot through onHost::transformReduce    (:337-345)
  *   scan_i32 / scan_u64  onHost::exclusiveScan / inclusiveScan with a caller buffer of getScanBufferSize bytes
  *                                                                                      (onHost/algo/scan.hpp:26-218)
  *   heat       StencilKernel, 16x16 chunks, 18x18 shared tile                           (heatEquation2D.cpp:134-176)
@@ -181,38 +181,22 @@ namespace
         auto const spec = onHost::FrameSpec{numFrames, uint32_t{512}, exec::gpuCuda};
         q.enqueue(spec, KernelBundle{ForEach{}, InitOp{}, a, b, c});
         cudaStream_t const s = streamOf(q);
-        std::vector<cudaEvent_t> ev(6);
-        for(auto& e : ev)
-            RCB_CUDA(cudaEventCreate(&e));
-        double sum[5] = {0, 0, 0, 0, 0};
-        double ga = kInitA, gb = kInitB, gc = kInitC;
-        int const total = o.warmup + o.steps;
-        for(int r = 0; r < total; ++r)
-        {
-            RCB_CUDA(cudaEventRecord(ev[0], s));
-            q.enqueue(spec, KernelBundle{ForEach{}, CopyOp{}, a, c});
-            RCB_CUDA(cudaEventRecord(ev[1], s));
-            q.enqueue(spec, KernelBundle{ForEach{}, MulOp{}, b, c});
-            RCB_CUDA(cudaEventRecord(ev[2], s));
-            q.enqueue(spec, KernelBundle{ForEach{}, AddOp{}, a, b, c});
-            RCB_CUDA(cudaEventRecord(ev[3], s));
-            q.enqueue(spec, KernelBundle{ForEach{}, TriadOp{}, a, b, c});
-            RCB_CUDA(cudaEventRecord(ev[4], s));
-            onHost::transformReduce(q, exec::gpuCuda, 0.0, out, std::plus{}, Product{}, a, b);
-            RCB_CUDA(cudaEventRecord(ev[5], s));
-            RCB_CUDA(cudaEventSynchronize(ev[5]));
-            if(r >= o.warmup)
-                for(int k = 0; k < 5; ++k)
-                {
-                    float ms = 0.f;
-                    RCB_CUDA(cudaEventElapsedTime(&ms, ev[k], ev[k + 1]));
-                    sum[k] += ms;
-                }
-            gc = ga;
-            gb = kScalar * gc;
-            gc = ga + gb;
-            ga = gb + kScalar * gc;
-        }
+        // each operation W + K times back to back, the K timed between two events (the same bracket as the other
+        // workloads); the arrays then hold a = b + s*c, b = s*c, c = a0 + b with a0 the initial a
+        double ms[5];
+        ms[0] = timeSteps(s, o.warmup, o.steps, [&](int) { q.enqueue(spec, KernelBundle{ForEach{}, CopyOp{}, a, c}); });
+        ms[1] = timeSteps(s, o.warmup, o.steps, [&](int) { q.enqueue(spec, KernelBundle{ForEach{}, MulOp{}, b, c}); });
+        ms[2] = timeSteps(s, o.warmup, o.steps, [&](int) { q.enqueue(spec, KernelBundle{ForEach{}, AddOp{}, a, b, c}); });
+        ms[3] = timeSteps(s, o.warmup, o.steps, [&](int) { q.enqueue(spec, KernelBundle{ForEach{}, TriadOp{}, a, b, c}); });
+        ms[4] = timeSteps(
+            s,
+            o.warmup,
+            o.steps,
+            [&](int) { onHost::transformReduce(q, exec::gpuCuda, 0.0, out, std::plus{}, Product{}, a, b); });
+        double const gc0 = kInitA;
+        double const gb = kScalar * gc0;
+        double const gc = kInitA + gb;
+        double const ga = gb + kScalar * gc;
         onHost::memcpy(q, outHost, out);
         onHost::wait(q);
         auto ha = onHost::allocHostLike(a);
@@ -238,10 +222,8 @@ namespace
         for(int k = 0; k < 5; ++k)
         {
             std::string const wl = std::string("babelstream_") + names[k];
-            emit(wl.c_str(), n, sum[k] / o.steps, bytes[k], "GB/s", o.steps, k == 4 ? dot : arrays);
+            emit(wl.c_str(), n, ms[k], bytes[k], "GB/s", o.steps, k == 4 ? dot : arrays);
         }
-        for(auto& e : ev)
-            RCB_CUDA(cudaEventDestroy(e));
     }
 
     // ---------------------------------------------------------------- scans
@@ -293,7 +275,11 @@ namespace
         using IdxVec = Vec<uint32_t, 2u>;
         uint32_t const n = o.small ? 512u : 32768u;
         IdxVec const numNodes{n, n};
-        IdxVec const extent{n + 2u, n + 2u};
+        // The buffers get 64-bit extents: MdSpan computes byte offsets in its index type (mem/MdSpan.hpp:267-282),
+        // and the example's uint32 extents (heatEquation2D.cpp:27) wrap past 4 GiB, which a 32768^2 fp64 field
+        // exceeds (with uint32 extents the field came out wrong on the B200 at this size).
+        using BufVec = Vec<uint64_t, 2u>;
+        BufVec const extent{n + 2ull, n + 2ull};
         double const dx = 1.0 / static_cast<double>(n + 1u);
         double const r = 0.2;
         double const dt = r * dx * dx;
@@ -306,7 +292,7 @@ namespace
             auto md = host.getMdSpan();
             for(uint32_t j = 0; j < n + 2u; ++j)
                 for(uint32_t i = 0; i < n + 2u; ++i)
-                    md[IdxVec{j, i}] = sx[j] * sx[i];
+                    md[BufVec{j, i}] = sx[j] * sx[i];
         }
         auto cur = onHost::alloc<double>(dev, extent);
         auto nxt = onHost::allocLike(dev, cur);
@@ -338,9 +324,9 @@ namespace
         for(uint32_t j : {1u, n / 3u, n / 2u, n})
             for(uint32_t i = 0; i < n + 2u; ++i)
             {
-                double const want = h0[IdxVec{j, i}] * std::pow(lambda, total);
-                err = std::max(err, std::fabs(md[IdxVec{j, i}] - want));
-                scale = std::max(scale, std::fabs(h0[IdxVec{j, i}]));
+                double const want = h0[BufVec{j, i}] * std::pow(lambda, total);
+                err = std::max(err, std::fabs(md[BufVec{j, i}] - want));
+                scale = std::max(scale, std::fabs(h0[BufVec{j, i}]));
             }
         char buf[96];
         std::snprintf(buf, sizeof(buf), "normwise error %.3e above 1e-12", err / scale);
