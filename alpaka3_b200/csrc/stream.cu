@@ -6,12 +6,13 @@
 // SimdIotaKernel / generic fill (include/alpaka/onHost/algo/internal/transform.hpp:21-107, concurrent.hpp:18-67,
 // iota.hpp:19-75, include/alpaka/api/generic.hpp:45-88).
 //
-// Design: the arrays are cut into chunks of 256 threads x 32 bytes per array (one 256-bit load/store instruction per
-// thread on sm_100 when every pointer is 32-byte aligned; two 16-byte packs when 16-byte aligned; single elements
-// otherwise), and block b handles chunk b: a full grid of short-lived blocks, which the block scheduler hands out in
-// index order, so the whole GPU sweeps memory front to back. On B200 this measured 5-7% faster than a resident grid
-// walking the arrays grid-stride (copy 6.55 vs 6.24 TB/s, triad 6.84 vs 6.50 TB/s on 2^25 fp64 arrays). Beyond 2^31
-// chunks (2^39 packs) the call is rejected.
+// Design: the arrays are cut into chunks of 512 threads x (1 or 2) 16-byte packs per array and block b handles
+// chunk b: a full grid of short-lived blocks, which the block scheduler hands out in index order, so the whole GPU
+// sweeps memory front to back. Operations that touch two arrays (copy, mul, map) move two packs per thread (16 KB
+// per array per block), those that touch three or four (add, triad, nstream) one (8 KB per array per block); these
+// shapes measured best on B200 among 16/32-byte packs, 128/256/512-thread blocks and 1-4 packs per thread (2^25
+// fp64: copy 6.70, add 6.98, triad 7.00 TB/s, against 6.24 / 6.50 TB/s for a resident grid walking the arrays
+// grid-stride). Pointers that are not 16-byte aligned are walked element by element in the same chunk shape.
 // Floating-point operations use explicitly rounded intrinsics, so results are bit-identical to an IEEE CPU
 // evaluation of the same expression without contraction.
 #include <type_traits>
@@ -22,19 +23,23 @@ namespace a3b
 {
     namespace
     {
-        constexpr int kBlock = 256;
+        constexpr int kBlock = 256;               // iota, generators, drift
+        constexpr int kStreamBlock = 512;         // element-wise chunk kernel
         constexpr uint64_t kMaxGrid = 1ull << 31; // gridDim.x limit
 
-        // packs per thread per chunk: 32 bytes of each array
-        template<typename T, int W>
+        // packs per thread per chunk: 32 bytes of each array for operations on two arrays, 16 bytes for three or four
+        template<typename T, int W, typename Op>
         __host__ __device__ constexpr int packsPerThread()
         {
-            constexpr int bytes = W * static_cast<int>(sizeof(T));
-            return bytes >= 32 ? 1 : 32 / bytes;
+            constexpr int mask = Op::R | Op::Wr;
+            constexpr int arrays = (mask & 1) + ((mask >> 1) & 1) + ((mask >> 2) & 1);
+            constexpr int bytes = arrays <= 2 ? 32 : 16;
+            constexpr int pack = W * static_cast<int>(sizeof(T));
+            return bytes / pack > 0 ? bytes / pack : 1;
         }
 
         template<typename T, int W>
-        struct alignas(W * sizeof(T) >= 32 ? 32 : 16) Pack
+        struct alignas(16) Pack
         {
             T v[W];
         };
@@ -83,21 +88,9 @@ namespace a3b
         template<typename T, int W>
         __device__ __forceinline__ Pack<T, W> loadPack(T const* base, uint64_t packIdx)
         {
-            if constexpr(W * sizeof(T) == 32)
+            if constexpr(W * sizeof(T) == 16)
             {
-                // 256-bit load (sm_100): one instruction per 32-byte pack
-                unsigned long long r0, r1, r2, r3;
-                asm volatile("ld.global.v4.u64 {%0, %1, %2, %3}, [%4];"
-                             : "=l"(r0), "=l"(r1), "=l"(r2), "=l"(r3)
-                             : "l"(base + packIdx * W));
-                unsigned long long raw[4] = {r0, r1, r2, r3};
-                Pack<T, W> p;
-                memcpy(&p, raw, 32);
-                return p;
-            }
-            else if constexpr(W * sizeof(T) == 16)
-            {
-                uint4 raw = __ldcs(reinterpret_cast<uint4 const*>(base) + packIdx);
+                uint4 raw = reinterpret_cast<uint4 const*>(base)[packIdx];
                 return *reinterpret_cast<Pack<T, W>*>(&raw);
             }
             else
@@ -113,17 +106,9 @@ namespace a3b
         template<typename T, int W>
         __device__ __forceinline__ void storePack(T* base, uint64_t packIdx, Pack<T, W> const& p)
         {
-            if constexpr(W * sizeof(T) == 32)
+            if constexpr(W * sizeof(T) == 16)
             {
-                unsigned long long raw[4];
-                memcpy(raw, &p, 32);
-                asm volatile("st.global.v4.u64 [%0], {%1, %2, %3, %4};" ::"l"(base + packIdx * W), "l"(raw[0]),
-                             "l"(raw[1]), "l"(raw[2]), "l"(raw[3])
-                             : "memory");
-            }
-            else if constexpr(W * sizeof(T) == 16)
-            {
-                __stcs(reinterpret_cast<uint4*>(base) + packIdx, *reinterpret_cast<uint4 const*>(&p));
+                reinterpret_cast<uint4*>(base)[packIdx] = *reinterpret_cast<uint4 const*>(&p);
             }
             else
             {
@@ -317,21 +302,21 @@ namespace a3b
             }
         }
 
-        // W elements per pack; block c covers packs [c * kBlock * U, (c + 1) * kBlock * U), thread t takes packs
-        // c * kBlock * U + u * kBlock + t (each warp instruction covers 32 consecutive packs). The grid has one block
-        // per chunk (at least one): a full chunk moves all its packs at once with no predicates, the last chunk
-        // checks each pack.
+        // W elements per pack; block c covers packs [c * kStreamBlock * U, (c + 1) * kStreamBlock * U), thread t
+        // takes packs c * kStreamBlock * U + u * kStreamBlock + t (each warp instruction covers 32 consecutive
+        // packs). The grid has one block per chunk (at least one): a full chunk moves all its packs at once with no
+        // predicates, the last chunk checks each pack.
         template<typename T, int W, typename Op>
-        __global__ void __launch_bounds__(kBlock) streamKernel(Op op, T* p0, T* p1, T* p2, uint64_t n)
+        __global__ void __launch_bounds__(kStreamBlock) streamKernel(Op op, T* p0, T* p1, T* p2, uint64_t n)
         {
-            constexpr int U = packsPerThread<T, W>();
+            constexpr int U = packsPerThread<T, W, Op>();
             uint64_t const nPacks = n / W;
-            uint64_t const chunk = static_cast<uint64_t>(kBlock) * U;
+            uint64_t const chunk = static_cast<uint64_t>(kStreamBlock) * U;
             uint64_t const c = blockIdx.x;
             uint64_t idx[U];
 #pragma unroll
             for(int u = 0; u < U; ++u)
-                idx[u] = c * chunk + static_cast<uint64_t>(u) * kBlock + threadIdx.x;
+                idx[u] = c * chunk + static_cast<uint64_t>(u) * kStreamBlock + threadIdx.x;
             if(c * chunk + chunk <= nPacks)
                 applyPacks<T, W, U>(op, p0, p1, p2, idx, U);
             else
@@ -347,7 +332,7 @@ namespace a3b
             if constexpr(W > 1)
             {
                 // tail elements after the last whole pack
-                uint64_t const t = static_cast<uint64_t>(blockIdx.x) * kBlock + threadIdx.x;
+                uint64_t const t = static_cast<uint64_t>(blockIdx.x) * kStreamBlock + threadIdx.x;
                 uint64_t const e = nPacks * W + t;
                 if(e < n)
                 {
@@ -371,10 +356,10 @@ namespace a3b
 
         // one block per chunk (at least one, so the tail elements of a pack-less array are handled); 0 when the
         // array needs more blocks than a grid holds (more than 2^39 packs)
-        template<typename T, int W>
+        template<typename T, int W, typename Op>
         unsigned gridFor(uint64_t n)
         {
-            uint64_t const chunk = static_cast<uint64_t>(kBlock) * packsPerThread<T, W>();
+            uint64_t const chunk = static_cast<uint64_t>(kStreamBlock) * packsPerThread<T, W, Op>();
             uint64_t const chunks = (n / W + chunk - 1) / chunk;
             if(chunks >= kMaxGrid)
                 return 0u;
@@ -396,20 +381,18 @@ namespace a3b
                 return (!(Op::R & 1 || Op::Wr & 1) || ok(p0)) && (!(Op::R & 2 || Op::Wr & 2) || ok(p1))
                        && (!(Op::R & 4 || Op::Wr & 4) || ok(p2));
             };
-            constexpr int W32 = 32 / sizeof(T), W16 = packWidth<T>();
-            bool const a32 = alignedTo(32), a16 = alignedTo(16);
-            unsigned const grid = a32 ? gridFor<T, W32>(n) : a16 ? gridFor<T, W16>(n) : gridFor<T, 1>(n);
+            constexpr int W16 = packWidth<T>();
+            bool const a16 = alignedTo(16);
+            unsigned const grid = a16 ? gridFor<T, W16, Op>(n) : gridFor<T, 1, Op>(n);
             if(grid == 0u)
             {
                 setError("array of %llu elements needs more blocks than a grid holds", static_cast<unsigned long long>(n));
                 return A3B_ERR_TOO_LARGE;
             }
-            if(a32)
-                streamKernel<T, W32, Op><<<grid, kBlock, 0, s>>>(op, p0, p1, p2, n);
-            else if(a16)
-                streamKernel<T, W16, Op><<<grid, kBlock, 0, s>>>(op, p0, p1, p2, n);
+            if(a16)
+                streamKernel<T, W16, Op><<<grid, kStreamBlock, 0, s>>>(op, p0, p1, p2, n);
             else
-                streamKernel<T, 1, Op><<<grid, kBlock, 0, s>>>(op, p0, p1, p2, n);
+                streamKernel<T, 1, Op><<<grid, kStreamBlock, 0, s>>>(op, p0, p1, p2, n);
             A3B_CHECK_LAUNCH("stream kernel launch");
             return A3B_OK;
         }
