@@ -483,6 +483,18 @@ namespace a3b
             return v;
         }
 
+        // peers.slots[q] for a run-time q without indexing the parameter array (a dynamic index would copy the
+        // whole struct to a per-thread stack frame in every block)
+        __device__ __forceinline__ unsigned long long* slotOf(PeerSlots const& peers, int q)
+        {
+            unsigned long long* r = peers.slots[0];
+#pragma unroll
+            for(int k = 1; k < kMaxPeers; ++k)
+                if(q == k)
+                    r = peers.slots[k];
+            return r;
+        }
+
         // Local reduction as reduceKernel; the last block then stores the unrounded local total into slot
         // [epoch parity][rank] of every rank's slot buffer (value, then the epoch with release semantics), waits for
         // the world's values in its own buffer and combines them in rank order: every rank computes the same bits.
@@ -521,7 +533,7 @@ namespace a3b
             bool const active = lane < peers.world;
             if(active)
             {
-                unsigned long long* slot = peers.slots[lane] + 2 * (par * kMaxPeers + peers.rank);
+                unsigned long long* slot = slotOf(peers, lane) + 2 * (par * kMaxPeers + peers.rank);
                 stRelaxedSys(slot, bits);
                 __threadfence_system(); // the value is visible to rank `lane` before the epoch that announces it
                 stRelaxedSys(slot + 1, peers.epoch);
@@ -530,7 +542,7 @@ namespace a3b
             unsigned long long vb = 0;
             if(active)
             {
-                unsigned long long const* slot = peers.slots[peers.rank] + 2 * (par * kMaxPeers + lane);
+                unsigned long long const* slot = slotOf(peers, peers.rank) + 2 * (par * kMaxPeers + lane);
                 uint64_t const t0 = globalTimerNs();
                 while(ldAcquireSys(slot + 1) != peers.epoch)
                 {
