@@ -256,7 +256,7 @@ def run_b200(args):
             "roofline": {"bound": "hbm", "achieved": round(kern_gbs, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(kern_gbs / peak, 4), "peak_kind": peak_kind,
                          "traffic": SUMSQ_TRAFFIC_PER_LAUNCH(n_local),
-                         "kernel": "reduceKernel<float,4,plus,square> (a3b_transform_reduce)",
+                         "kernel": "reduceKernel<float, 8 per pack, plus, square> (a3b_transform_reduce)",
                          "kernel_ms": round(kern_ms, 5)},
             "e2e": e2e, "gpu_launches": launches[0], "clocks": sampler.summary(),
         }

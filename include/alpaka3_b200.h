@@ -170,8 +170,8 @@ A3B_API int a3b_transform_reduce_partial(a3b_stream_t stream, int dtype, int red
  * whose device memory is owned by another allocator's pool, a service that must keep a fixed, accounted memory
  * footprint, a latency-critical loop that cannot afford an allocation's implicit synchronisation. Same arguments and result
  * as a3b_transform_reduce over a dense 1-D input; it allocates nothing. Its scratch is one fixed 16 KB static device
- * array per GPU that loads the library (held until the process exits): a 64-byte header plus one 8-byte partial per
- * block, i.e. at most 2040 blocks; a device/size that would need more is rejected with A3B_ERR_TOO_LARGE. The first
+ * array per GPU that loads the library (held until the process exits): the tickets and partials of at most 2024 blocks,
+ * each of which takes several chunks of a large input (A3B_ERR_TOO_LARGE is kept for a layout that would not fit). The first
  * call on a device looks up that array's device address, so make the first call before any stream capture. All
  * calls share the array: calls that overlap on the GPU (different streams, devices' own streams in parallel) race
  * and must be serialised by the caller. */
