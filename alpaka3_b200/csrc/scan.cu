@@ -1,26 +1,35 @@
-// Single-pass prefix sum (decoupled look-back): onHost::inclusiveScan / exclusiveScan / *InPlace.
+// Single-pass prefix sum with aggregates published ahead: onHost::inclusiveScan / exclusiveScan / *InPlace.
 //
 // Replaces the three-level Scan_ScanBlocksKernel + recursion + Scan_AddIncrementsKernel scheme of
 // include/alpaka/onHost/algo/internal/scan.hpp:114-472 (about 4N-5N elements of traffic and 2*levels launches) with
-// one launch that reads every element once and writes it once (2N).
+// one launch that reads every element from HBM once and writes it once (2N).
 //
-// One block per tile (tile = blockIdx.x; blocks are dispatched in index order, so every predecessor a tile waits for
-// is resident or finished). A tile is 256 threads x ROUNDS 16-byte packs held in registers: 48 KB (12 rounds) for
-// 4-byte and 64 KB (16 rounds) for 8-byte types, the largest tiles that keep 3 / 2 blocks resident per SM; larger
-// tiles mean fewer look-backs per byte. Warp w owns a contiguous segment; in round r lane l holds the pack at segment
-// offset (r*32 + l), so every load and store instruction of a warp covers 512 contiguous bytes. Scans run in
-// registers: within the pack, across lanes (shfl_up), across rounds (running segment total), across the 8 warps
-// (shared memory), then across tiles. Unaligned input or output uses the same kernel with per-element loads.
+// One block per tile (tile = blockIdx.x; blocks are dispatched in index order, so every block a tile waits for is
+// resident or finished). A tile is 256 threads x 16 packs of 16 bytes (64 KB), two blocks per SM. Warp w owns a
+// contiguous segment; in round r lane l holds the pack at segment offset (r*32 + l), so every load and store
+// instruction of a warp covers 512 contiguous bytes. Scans run in registers: within the pack, across lanes
+// (shfl_up), across rounds (running segment total), across the 8 warps (shared memory), then across tiles.
 //
-// Cross-tile protocol: a tile publishes its aggregate (flag A), then the WHOLE block looks back: thread i polls the
-// predecessors at distance i, i + 256, ... so one L2 round trip covers a window of kLookSpan tiles, more than a
-// launch keeps in flight. The window is complete as soon as every predecessor up to the nearest inclusive prefix
-// (flag P) is valid; the tile then publishes its own inclusive prefix. Status words carry an epoch handed out by the
-// host per call on the stream's cached scratch (a caller buffer is cleared and uses epoch 1), so the scratch needs no
-// clearing between calls. A status is one 64-bit word per 32 bits of value: flag (2 bits) | epoch (30 bits) | 32
-// value bits; relaxed 64-bit accesses are single-copy atomic, and an 8-byte value's two words are accepted only when
-// both carry the same flag and epoch. Every spin is bounded by %globaltimer; on timeout the block raises the device
-// error word and an abort mark that ends the other blocks' waits of the same call.
+// Aggregates ahead of prefixes. In a plain decoupled look-back a tile's prefix waits until every predecessor up to
+// the nearest inclusive prefix has loaded its tile from HBM, and the waiting blocks hold their tiles on chip; at full
+// HBM load that wait (several L2 round trips behind loads still in flight) limits the scan to ~60% of the copy rate.
+// Here block b also reduces tile b + lag: at its start one thread issues a TMA bulk copy of that tile into shared
+// memory, and after block b has written its own tile it sums the staged tile and publishes it as the aggregate of
+// tile b + lag. By the time block b + lag runs, the aggregates of all its recent predecessors are long published, so
+// its look-back resolves in its first poll (whose status words it loads before its own tile), and its own tile (read
+// by the TMA copy a few microseconds earlier) is served from L2: HBM still sees one read and one write per element.
+// lag = 2 x the resident blocks of the launch keeps the in-between window (lag tiles, ~40 MB) well inside the 126 MB
+// L2. Tiles below lag publish their own aggregate. Aggregates and inclusive prefixes live in separate status arrays,
+// so every status word has one writer. When input and output overlap (in-place scan), block b waits until the
+// aggregate of its tile is published, i.e. until the ahead copy has read the tile, before it overwrites it.
+//
+// Status words carry an epoch handed out by the host per call on the stream's cached scratch (a caller buffer is
+// cleared and uses epoch 1), so the scratch needs no clearing between calls. A status is one 64-bit word per 32 bits
+// of value: flag (2 bits) | epoch (30 bits) | 32 value bits; relaxed 64-bit accesses are single-copy atomic, and an
+// 8-byte value's two words are accepted only when both carry the same flag and epoch. Every spin is bounded by
+// %globaltimer; on timeout the block raises the device error word and an abort mark that ends the other blocks'
+// waits of the same call. Input or output not aligned to 16 bytes uses the same kernel with per-element loads and
+// no TMA.
 #include <type_traits>
 
 #include "common.cuh"
@@ -31,10 +40,7 @@ namespace a3b
     {
         constexpr int kBlock = 256;
         constexpr int kWarps = kBlock / 32;
-#ifndef A3B_SCAN_LOOKSPAN
-#define A3B_SCAN_LOOKSPAN 512
-#endif
-        constexpr int kLookSpan = A3B_SCAN_LOOKSPAN; // predecessors polled per look-back window (multiple of 256)
+        constexpr int kLookSpan = 512; // predecessors polled per look-back window (multiple of 256)
         constexpr unsigned kEpochMask = 0x3FFFFFFFu;
         constexpr unsigned kFlagA = 1u, kFlagP = 2u;
 
@@ -45,23 +51,65 @@ namespace a3b
         };
         static_assert(sizeof(ScanHeader) == 64, "header size");
 
-        // Tile shape per element size (measured on B200): 48 KB tiles for 4-byte and 64 KB tiles for 8-byte types
-        // (12 / 16 rounds of one 16-byte pack per thread), the largest that keep 3 / 2 blocks resident per SM.
-        template<int ES>
-        constexpr int roundsFor()
-        {
-            return ES == 4 ? 12 : 16;
-        }
-
+#ifndef A3B_SCAN_ROUNDS
+#define A3B_SCAN_ROUNDS 16
+#endif
+#ifndef A3B_SCAN_MINB
+#define A3B_SCAN_MINB 2
+#endif
+#ifndef A3B_SCAN_PACK
+#define A3B_SCAN_PACK 16
+#endif
         template<typename T>
         struct Traits
         {
-            static constexpr int W = 16 / static_cast<int>(sizeof(T));    // elements per 16-byte pack
-            static constexpr int ROUNDS = roundsFor<sizeof(T)>();         // packs per thread
+            static constexpr int PB = A3B_SCAN_PACK;                      // bytes per pack (one 256-bit access)
+            static constexpr int W = PB / static_cast<int>(sizeof(T));    // elements per pack
+            static constexpr int ROUNDS = A3B_SCAN_ROUNDS;                // packs per thread
             static constexpr int TILE = kBlock * ROUNDS * W;              // elements per tile
+            static constexpr int STAGE = kBlock * ROUNDS * PB;            // bytes per tile
             static constexpr int WORDS = static_cast<int>(sizeof(T)) / 4; // 64-bit status words per tile
-            static constexpr int MIN_BLOCKS = ROUNDS <= 8 ? 4 : (ROUNDS <= 12 ? 3 : 2);
+            static constexpr int MIN_BLOCKS = A3B_SCAN_MINB;
         };
+
+        // one pack of global memory <-> registers, evict-first (each element is read once and written once here)
+        template<int PB>
+        __device__ __forceinline__ void loadPack(void const* p, uint32_t (&w)[PB / 4])
+        {
+            if constexpr(PB == 32)
+            {
+                unsigned long long r0, r1, r2, r3;
+                asm volatile("ld.global.cs.v4.u64 {%0, %1, %2, %3}, [%4];"
+                             : "=l"(r0), "=l"(r1), "=l"(r2), "=l"(r3)
+                             : "l"(p));
+                unsigned long long const raw[4] = {r0, r1, r2, r3};
+                memcpy(w, raw, 32);
+            }
+            else
+            {
+                uint4 const v = __ldcs(static_cast<uint4 const*>(p));
+                memcpy(w, &v, 16);
+            }
+        }
+
+        template<int PB>
+        __device__ __forceinline__ void storePack(void* p, uint32_t const (&w)[PB / 4])
+        {
+            if constexpr(PB == 32)
+            {
+                unsigned long long raw[4];
+                memcpy(raw, w, 32);
+                asm volatile("st.global.cs.v4.u64 [%0], {%1, %2, %3, %4};" ::"l"(p), "l"(raw[0]), "l"(raw[1]),
+                             "l"(raw[2]), "l"(raw[3])
+                             : "memory");
+            }
+            else
+            {
+                uint4 v;
+                memcpy(&v, w, 16);
+                __stcs(static_cast<uint4*>(p), v);
+            }
+        }
 
         template<typename T>
         __device__ __forceinline__ T add(T a, T b)
@@ -79,18 +127,24 @@ namespace a3b
             return (x + 255u) & ~size_t{255u};
         }
 
-        // scratch layout: header | u64 status[tiles * WORDS]
+        // scratch layout: header | u64 aggregate[tiles * WORDS] | u64 inclusive[tiles * WORDS]
+        __host__ __device__ inline size_t statusBytes(uint64_t tiles, int words)
+        {
+            return align256(tiles * 8u * static_cast<uint64_t>(words));
+        }
+
         __host__ __device__ inline size_t scratchBytes(uint64_t tiles, int words)
         {
-            return sizeof(ScanHeader) + align256(tiles * 8u * static_cast<uint64_t>(words));
+            return sizeof(ScanHeader) + 2u * statusBytes(tiles, words);
         }
 
         template<typename T>
         struct Status
         {
-            uint64_t* word;
+            uint64_t* agg; // aggregate of each tile (flag A), written once per call
+            uint64_t* inc; // inclusive prefix of each tile (flag P), written once per call
 
-            __device__ void publish(uint64_t tile, unsigned flag, unsigned epoch, T value) const
+            __device__ static void put(uint64_t* base, uint64_t tile, unsigned flag, unsigned epoch, T value)
             {
                 constexpr int WD = Traits<T>::WORDS;
                 uint32_t parts[WD];
@@ -98,30 +152,82 @@ namespace a3b
                 uint64_t const tag = (static_cast<uint64_t>(flag) << 62) | (static_cast<uint64_t>(epoch) << 32);
 #pragma unroll
                 for(int k = 0; k < WD; ++k)
-                    stRelaxedU64(word + tile * WD + k, tag | parts[k]);
+                    stRelaxedU64(base + tile * WD + k, tag | parts[k]);
             }
 
-            // flag seen for `tile` in this epoch (0 = not yet, or the words of an 8-byte value disagree) and its value
-            __device__ unsigned peek(uint64_t tile, unsigned epoch, T& value) const
+            // true when all words of w carry this epoch's tag; value decoded
+            __device__ static bool decode(uint64_t const (&w)[Traits<T>::WORDS], unsigned epoch, T& value)
             {
                 constexpr int WD = Traits<T>::WORDS;
-                uint64_t w[WD];
-#pragma unroll
-                for(int k = 0; k < WD; ++k)
-                    w[k] = ldRelaxedU64(word + tile * WD + k);
                 unsigned const tag = static_cast<unsigned>(w[0] >> 32);
                 if((tag & kEpochMask) != epoch)
-                    return 0u;
+                    return false;
                 uint32_t parts[WD];
 #pragma unroll
                 for(int k = 0; k < WD; ++k)
                 {
                     if(static_cast<unsigned>(w[k] >> 32) != tag)
-                        return 0u;
+                        return false;
                     parts[k] = static_cast<uint32_t>(w[k]);
                 }
                 memcpy(&value, parts, sizeof(T));
-                return tag >> 30;
+                return true;
+            }
+
+            __device__ void publishA(uint64_t tile, unsigned epoch, T value) const
+            {
+                put(agg, tile, kFlagA, epoch, value);
+            }
+
+            __device__ void publishP(uint64_t tile, unsigned epoch, T value) const
+            {
+                put(inc, tile, kFlagP, epoch, value);
+            }
+
+            // raw status words of one tile, as loaded
+            struct Raw
+            {
+                uint64_t i[Traits<T>::WORDS];
+                uint64_t a[Traits<T>::WORDS];
+            };
+
+            __device__ void load(uint64_t tile, Raw& r) const
+            {
+                constexpr int WD = Traits<T>::WORDS;
+#pragma unroll
+                for(int k = 0; k < WD; ++k)
+                {
+                    r.i[k] = ldRelaxedU64(inc + tile * WD + k);
+                    r.a[k] = ldRelaxedU64(agg + tile * WD + k);
+                }
+            }
+
+            // kFlagP with the inclusive prefix, else kFlagA with the aggregate, else 0 (not yet published)
+            __device__ static unsigned classify(Raw const& r, unsigned epoch, T& value)
+            {
+                if(decode(r.i, epoch, value))
+                    return kFlagP;
+                if(decode(r.a, epoch, value))
+                    return kFlagA;
+                return 0u;
+            }
+
+            __device__ unsigned peek(uint64_t tile, unsigned epoch, T& value) const
+            {
+                Raw r;
+                load(tile, r);
+                return classify(r, epoch, value);
+            }
+
+            __device__ bool aggPublished(uint64_t tile, unsigned epoch) const
+            {
+                constexpr int WD = Traits<T>::WORDS;
+                uint64_t wa[WD];
+#pragma unroll
+                for(int k = 0; k < WD; ++k)
+                    wa[k] = ldRelaxedU64(agg + tile * WD + k);
+                T v;
+                return decode(wa, epoch, v);
             }
         };
 
@@ -139,19 +245,49 @@ namespace a3b
         struct Shared
         {
             T warpTotal[kWarps];
+            T aheadTotal[kWarps];
             T red[kWarps];
             int firstP[kLookSpan / 32];
             int firstInv[kLookSpan / 32];
             int abort;
+            alignas(8) unsigned long long mbar;
         };
 
-        // Block-wide look-back for `tile` (> 0) whose aggregate is already published; returns the exclusive prefix.
-        // One window covers kLookSpan predecessors: thread i polls predecessors at distance i, i + 256, ... so a
-        // single L2 round trip spans more tiles than a launch keeps in flight (the distance to the nearest published
-        // inclusive prefix stays inside one window). A window is complete as soon as every predecessor up to the
-        // nearest inclusive prefix is valid (stragglers farther back do not matter); without a prefix in the window
-        // all of it must be valid and the window moves back. Sets sh.abort (and the error word) when a wait gives up.
+        __device__ __forceinline__ bool abortRequested(ScanHeader* hdr, unsigned epoch, uint64_t t0, uint64_t timeoutNs)
+        {
+            return (globalTimerNs() - t0 > timeoutNs) || (ldRelaxedU32(&hdr->abortEpoch) == epoch);
+        }
+
+        __device__ __forceinline__ void raiseAbort(ScanHeader* hdr, unsigned epoch, unsigned* errWord)
+        {
+            atomicOr(errWord, kErrTimeout);
+            stRelaxedU32(&hdr->abortEpoch, epoch);
+        }
+
+        // Block-wide look-back for `tile` (> 0); returns the exclusive prefix. One window covers kLookSpan
+        // predecessors: thread i polls predecessors at distance i, i + 256, ... so a single L2 round trip spans more
+        // tiles than a launch keeps in flight. A window is complete as soon as every predecessor up to the nearest
+        // inclusive prefix is valid (stragglers farther back do not matter); without a prefix in the window all of
+        // it must be valid and the window moves back. Sets sh.abort (and the error word) when a wait gives up.
+        constexpr int kLookQ = kLookSpan / kBlock; // predecessors per thread and window
+
+        // the first window's status words, loaded before the block's own tile so that they are not queued behind it
         template<typename T>
+        __device__ __forceinline__ void prefetchWindow(
+            Status<T> const& st,
+            uint64_t tile,
+            typename Status<T>::Raw (&pre)[kLookQ])
+        {
+#pragma unroll
+            for(int q = 0; q < kLookQ; ++q)
+            {
+                int64_t const j = static_cast<int64_t>(tile) - 1 - static_cast<int64_t>(threadIdx.x) - q * kBlock;
+                if(j >= 0)
+                    st.load(static_cast<uint64_t>(j), pre[q]);
+            }
+        }
+
+        template<typename T, bool PRE>
         __device__ T lookBack(
             Status<T> const& st,
             uint64_t tile,
@@ -159,9 +295,10 @@ namespace a3b
             Shared<T>& sh,
             ScanHeader* hdr,
             unsigned* errWord,
-            uint64_t timeoutNs)
+            uint64_t timeoutNs,
+            typename Status<T>::Raw const (&pre)[kLookQ])
         {
-            constexpr int Q = kLookSpan / kBlock;
+            constexpr int Q = kLookQ;
             int const warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
             uint64_t const t0 = globalTimerNs();
             int64_t pred = static_cast<int64_t>(tile) - 1;
@@ -180,12 +317,15 @@ namespace a3b
                     flag[q] = j[q] >= 0 ? 0u : kFlagP; // before tile 0: an empty inclusive prefix
                 }
                 int stop;
+                bool firstPoll = PRE && pred == static_cast<int64_t>(tile) - 1;
                 while(true)
                 {
 #pragma unroll
                     for(int q = 0; q < Q; ++q)
-                        if(flag[q] == 0u)
-                            flag[q] = st.peek(static_cast<uint64_t>(j[q]), epoch, val[q]);
+                        if(flag[q] != kFlagP)
+                            flag[q] = firstPoll ? Status<T>::classify(pre[q], epoch, val[q])
+                                                : st.peek(static_cast<uint64_t>(j[q]), epoch, val[q]);
+                    firstPoll = false;
 #pragma unroll
                     for(int q = 0; q < Q; ++q)
                     {
@@ -212,7 +352,7 @@ namespace a3b
                     if(stop < kLookSpan ? inv > stop : inv == kLookSpan)
                         break;
                     if(threadIdx.x == 0 && (++polls & 7) == 0)
-                        sh.abort = (globalTimerNs() - t0 > timeoutNs) || (ldRelaxedU32(&hdr->abortEpoch) == epoch);
+                        sh.abort = abortRequested(hdr, epoch, t0, timeoutNs);
                     __syncthreads(); // firstP / firstInv are rewritten by the next poll
                     if(sh.abort)
                         break;
@@ -241,10 +381,7 @@ namespace a3b
                 pred -= kLookSpan;
             }
             if(sh.abort && threadIdx.x == 0)
-            {
-                atomicOr(errWord, kErrTimeout);
-                stRelaxedU32(&hdr->abortEpoch, epoch);
-            }
+                raiseAbort(hdr, epoch, errWord);
             return acc;
         }
 
@@ -289,14 +426,136 @@ namespace a3b
             run = add(run, roundTotal);
         }
 
-        // ---------------------------------------------------------------- one tile per block, data in registers
-        // Tile = blockIdx.x: blocks are dispatched in index order, so every predecessor a block waits for is already
-        // resident (the bounded waits turn any violation into a reported timeout, never a hang).
+        // Total of one warp-segment round, combined in exactly the order scanRound combines it (so a tile's
+        // aggregate has the same bits whether the ahead reduction or the tile's own scan computes it).
+        template<typename T>
+        __device__ __forceinline__ T roundTotal(T const (&p)[Traits<T>::W])
+        {
+            constexpr int W = Traits<T>::W;
+            int const lane = threadIdx.x & 31;
+            T x = p[0];
+#pragma unroll
+            for(int k = 1; k < W; ++k)
+                x = add(x, p[k]);
+#pragma unroll
+            for(int d = 1; d < 32; d <<= 1)
+            {
+                T const y = __shfl_up_sync(0xffffffffu, x, d);
+                if(lane >= d)
+                    x = add(y, x);
+            }
+            return __shfl_sync(0xffffffffu, x, 31);
+        }
+
+        // ------------------------------------------------------------------------------ TMA bulk copy + mbarrier
+        __device__ __forceinline__ uint32_t smemAddr(void const* p)
+        {
+            return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+        }
+
+        __device__ __forceinline__ void mbarInit(uint32_t bar, unsigned count)
+        {
+            asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        }
+
+        __device__ __forceinline__ void mbarExpectTx(uint32_t bar, unsigned bytes)
+        {
+            asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+        }
+
+        // global -> shared bulk copy of `bytes` (multiple of 16, both addresses 16-byte aligned), completing on `bar`
+        __device__ __forceinline__ void bulkLoad(uint32_t dst, void const* src, unsigned bytes, uint32_t bar)
+        {
+            asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+                         ::"r"(dst), "l"(src), "r"(bytes), "r"(bar)
+                         : "memory");
+        }
+
+        __device__ __forceinline__ bool mbarTryWait(uint32_t bar, unsigned parity)
+        {
+            unsigned done;
+            asm volatile(
+                "{\n\t.reg .pred p;\n\t"
+                "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+                "selp.u32 %0, 1, 0, p;\n\t}"
+                : "=r"(done)
+                : "r"(bar), "r"(parity)
+                : "memory");
+            return done != 0u;
+        }
+
+        // bounded wait for phase 0 of `bar`; false when `timeoutNs` passed first
+        __device__ bool mbarWaitBounded(uint32_t bar, uint64_t timeoutNs)
+        {
+            uint64_t const t0 = globalTimerNs();
+            while(!mbarTryWait(bar, 0u))
+                if(globalTimerNs() - t0 > timeoutNs)
+                    return false;
+            return true;
+        }
+
+        // Sum of a staged tile (Traits<T>::STAGE bytes in shared memory) in the order the tile's own scan combines
+        // it, so that the aggregate has the same bits either way; integer sums wrap and need no particular order.
+        template<typename T>
+        __device__ __forceinline__ T stagedTotal(uint4 const* stage, Shared<T>& sh)
+        {
+            using Tr = Traits<T>;
+            constexpr int W = Tr::W, R = Tr::ROUNDS;
+            int const warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+            T run = T(0);
+            if constexpr(std::is_integral_v<T>)
+            {
+                // conflict-free: thread i reads the 16-byte words i, i + 256, ...
+                constexpr int N16 = Tr::STAGE / 16 / kBlock;
+                uint64_t acc = 0u;
+#pragma unroll
+                for(int k = 0; k < N16; ++k)
+                {
+                    uint4 const q = stage[k * kBlock + threadIdx.x];
+                    if constexpr(sizeof(T) == 4)
+                        acc += static_cast<uint64_t>(q.x) + q.y + q.z + q.w;
+                    else
+                        acc += (static_cast<uint64_t>(q.y) << 32 | q.x) + (static_cast<uint64_t>(q.w) << 32 | q.z);
+                }
+                run = static_cast<T>(acc);
+                run = warpSum(run);
+            }
+            else
+            {
+                uint4 const* seg = stage + warp * (32 * R * Tr::PB / 16);
+#pragma unroll
+                for(int r = 0; r < R; ++r)
+                {
+                    T p[W];
+                    memcpy(&p[0], seg + (r * 32 + lane) * (Tr::PB / 16), Tr::PB);
+                    run = add(run, roundTotal<T>(p));
+                }
+            }
+            if(lane == 0)
+                sh.aheadTotal[warp] = run;
+            __syncthreads();
+            T total = T(0);
+#pragma unroll
+            for(int w = 0; w < kWarps; ++w)
+                total = add(total, sh.aheadTotal[w]);
+            return total;
+        }
+
+        // ------------------------------------------------------------------------------------------- the kernel
+        // Tile = blockIdx.x. Block b: (1) issues the TMA copy of tile b + lag into shared memory, (2) loads its own
+        // tile into registers, (3) looks back (b >= lag: while its loads are in flight; b < lag: after publishing its
+        // own aggregate), scans and publishes its inclusive prefix, (4) writes its tile, (5) sums the staged tile
+        // b + lag and publishes that aggregate. VEC: input and output aligned to the pack size (TMA and 32-byte
+        // packs); otherwise per-element accesses and no TMA.
         template<typename T, bool INCL, bool VEC>
         __global__ void __launch_bounds__(kBlock, Traits<T>::MIN_BLOCKS) scanTileKernel(
             T const* in,
             T* out,
             uint64_t n,
+            uint64_t tiles,
+            uint64_t lag,
+            int overlap,
             T const* carryIn,
             ScanHeader* hdr,
             unsigned epoch,
@@ -306,30 +565,57 @@ namespace a3b
         {
             using Tr = Traits<T>;
             constexpr int W = Tr::W;
+            constexpr int R = Tr::ROUNDS;
+            constexpr int PW = Tr::PB / 4; // 32-bit words per pack
+            extern __shared__ __align__(128) uint4 stage[]; // the ahead tile (VEC only): Tr::STAGE bytes
             __shared__ Shared<T> sh;
             int const warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
             uint64_t const tile = blockIdx.x;
-            if(threadIdx.x == 0)
-                sh.abort = 0;
-            Status<T> const st{reinterpret_cast<uint64_t*>(hdr + 1)};
+            Status<T> const st{
+                reinterpret_cast<uint64_t*>(hdr + 1),
+                reinterpret_cast<uint64_t*>(reinterpret_cast<unsigned char*>(hdr + 1) + statusBytes(tiles, Tr::WORDS))};
 
-            constexpr int kRounds = Tr::ROUNDS;
-            uint64_t const segBase = tile * Tr::TILE + static_cast<uint64_t>(warp) * (32 * kRounds * W);
+            // (1) ahead copy
+            uint64_t const ahead = tile + lag;
+            bool const doAhead = lag != 0 && ahead < tiles;
+            bool const aheadTma = VEC && doAhead && (ahead + 1u) * Tr::TILE <= n;
+            uint32_t const bar = smemAddr(&sh.mbar);
+            if(threadIdx.x == 0)
+            {
+                sh.abort = 0;
+                if(aheadTma)
+                {
+                    mbarInit(bar, 1u);
+                    mbarExpectTx(bar, Tr::STAGE);
+                    bulkLoad(smemAddr(stage), in + ahead * Tr::TILE, Tr::STAGE, bar);
+                }
+            }
+
+            // (2) own tile. A tile whose aggregate an earlier block publishes (tile >= lag) finds its predecessors'
+            // aggregates published already: its first look-back window is loaded before the tile and evaluated while
+            // the tile's loads are in flight.
+            bool const stalled = (tile == stallTile);
+            bool const ownAgg = lag == 0 || tile < lag; // else block tile - lag publishes it
+            typename Status<T>::Raw pre[kLookQ];
+            if(tile != 0 && !ownAgg)
+                prefetchWindow<T>(st, tile, pre);
+            uint64_t const segBase = tile * Tr::TILE + static_cast<uint64_t>(warp) * (32 * R * W);
             bool const full = (tile + 1u) * Tr::TILE <= n;
-            T v[kRounds][W];
+            T v[R][W];
             if(VEC && full)
             {
 #pragma unroll
-                for(int r = 0; r < kRounds; ++r)
+                for(int r = 0; r < R; ++r)
                 {
-                    uint4 raw = __ldcs(reinterpret_cast<uint4 const*>(in + segBase) + (r * 32 + lane));
-                    memcpy(&v[r][0], &raw, 16);
+                    uint32_t w[PW];
+                    loadPack<Tr::PB>(in + segBase + static_cast<uint64_t>(r * 32 + lane) * W, w);
+                    memcpy(&v[r][0], w, Tr::PB);
                 }
             }
             else
             {
 #pragma unroll
-                for(int r = 0; r < kRounds; ++r)
+                for(int r = 0; r < R; ++r)
 #pragma unroll
                     for(int k = 0; k < W; ++k)
                     {
@@ -337,9 +623,14 @@ namespace a3b
                         v[r][k] = idx < n ? in[idx] : T(0);
                     }
             }
+
+            // (3) prefix and scan
+            T prefix = T(0);
+            if(tile != 0 && !ownAgg)
+                prefix = lookBack<T, true>(st, tile, epoch, sh, hdr, errWord, timeoutNs, pre);
             T run = T(0);
 #pragma unroll
-            for(int r = 0; r < kRounds; ++r)
+            for(int r = 0; r < R; ++r)
                 scanRound<T, INCL>(v[r], run);
             if(lane == 0)
                 sh.warpTotal[warp] = run;
@@ -353,39 +644,58 @@ namespace a3b
                     warpPrefix = add(warpPrefix, t);
                 agg = add(agg, t);
             }
-            bool const stalled = (tile == stallTile);
-            T prefix = T(0);
             if(tile == 0)
             {
                 if(carryIn)
                     prefix = *carryIn;
             }
-            else
+            else if(ownAgg)
             {
                 if(threadIdx.x == 0 && !stalled)
-                    st.publish(tile, kFlagA, epoch, agg);
-                prefix = lookBack<T>(st, tile, epoch, sh, hdr, errWord, timeoutNs);
+                    st.publishA(tile, epoch, agg);
+                prefix = lookBack<T, false>(st, tile, epoch, sh, hdr, errWord, timeoutNs, pre);
             }
             if(threadIdx.x == 0 && !stalled)
-                st.publish(tile, kFlagP, epoch, add(prefix, agg));
+                st.publishP(tile, epoch, add(prefix, agg));
+            if(overlap && !ownAgg)
+            {
+                // in place: the ahead copy of block tile - lag must have read this tile before it is overwritten
+                if(threadIdx.x == 0)
+                {
+                    uint64_t const t0 = globalTimerNs();
+                    int polls = 0;
+                    while(!sh.abort && !st.aggPublished(tile, epoch))
+                    {
+                        if((++polls & 7) == 0 && abortRequested(hdr, epoch, t0, timeoutNs))
+                        {
+                            sh.abort = 1;
+                            raiseAbort(hdr, epoch, errWord);
+                        }
+                        __nanosleep(64);
+                    }
+                }
+                __syncthreads();
+            }
+
+            // (4) own output
             T const off = add(prefix, warpPrefix);
             if(VEC && full)
             {
 #pragma unroll
-                for(int r = 0; r < kRounds; ++r)
+                for(int r = 0; r < R; ++r)
                 {
 #pragma unroll
                     for(int k = 0; k < W; ++k)
                         v[r][k] = add(off, v[r][k]);
-                    uint4 raw;
-                    memcpy(&raw, &v[r][0], 16);
-                    __stcs(reinterpret_cast<uint4*>(out + segBase) + (r * 32 + lane), raw);
+                    uint32_t w[PW];
+                    memcpy(w, &v[r][0], Tr::PB);
+                    storePack<Tr::PB>(out + segBase + static_cast<uint64_t>(r * 32 + lane) * W, w);
                 }
             }
             else
             {
 #pragma unroll
-                for(int r = 0; r < kRounds; ++r)
+                for(int r = 0; r < R; ++r)
 #pragma unroll
                     for(int k = 0; k < W; ++k)
                     {
@@ -394,12 +704,117 @@ namespace a3b
                             out[idx] = add(off, v[r][k]);
                     }
             }
+
+            // (5) aggregate of tile + lag
+            if(!doAhead)
+                return;
+            T aa = T(0);
+            bool ok = true;
+            if(aheadTma)
+            {
+                ok = mbarWaitBounded(bar, timeoutNs);
+                if(!ok)
+                {
+                    // the copy still owns the staging buffer: give it one more bounded wait before the block exits
+                    if(threadIdx.x == 0)
+                        atomicOr(errWord, kErrTimeout);
+                    mbarWaitBounded(bar, timeoutNs);
+                }
+                ok = __syncthreads_and(ok) != 0; // publish only when every thread saw the staged tile
+                if(ok)
+                    aa = stagedTotal<T>(stage, sh);
+            }
+            else
+            {
+                uint64_t const aBase = ahead * Tr::TILE + static_cast<uint64_t>(warp) * (32 * R * W);
+                T aheadRun = T(0);
+#pragma unroll
+                for(int r = 0; r < R; ++r)
+                {
+                    T p[W];
+#pragma unroll
+                    for(int k = 0; k < W; ++k)
+                    {
+                        uint64_t const idx = aBase + static_cast<uint64_t>(r * 32 + lane) * W + k;
+                        p[k] = idx < n ? in[idx] : T(0);
+                    }
+                    aheadRun = add(aheadRun, roundTotal<T>(p));
+                }
+                if(lane == 0)
+                    sh.aheadTotal[warp] = aheadRun;
+                __syncthreads();
+#pragma unroll
+                for(int w = 0; w < kWarps; ++w)
+                    aa = add(aa, sh.aheadTotal[w]);
+            }
+            if(threadIdx.x == 0 && ok && ahead != stallTile)
+                st.publishA(ahead, epoch, aa);
         }
 
         template<typename T>
         uint64_t tilesFor(uint64_t n)
         {
             return (n + Traits<T>::TILE - 1) / Traits<T>::TILE;
+        }
+
+        // per-device launch data of one kernel instantiation: resident blocks per SM (0 = not set up yet)
+        template<typename T, bool INCL, bool VEC>
+        int kernelResident(DeviceProps const* props, int* resident)
+        {
+            static std::atomic<int> cache[kMaxDevices];
+            int r = cache[props->ordinal].load(std::memory_order_relaxed);
+            if(r == 0)
+            {
+                auto kernel = scanTileKernel<T, INCL, VEC>;
+                int const dyn = VEC ? Traits<T>::STAGE : 0;
+                if(dyn > 0)
+                    A3B_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, dyn));
+                int b = 0;
+                A3B_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b, kernel, kBlock, dyn));
+                r = b > 0 ? b : 1;
+                cache[props->ordinal].store(r, std::memory_order_relaxed);
+            }
+            *resident = r;
+            return A3B_OK;
+        }
+
+        // Tiles between a tile and the block that reduces it ahead: 2 x the blocks the launch keeps resident
+        // (A3B_SCAN_LAG overrides it for tuning; 0 turns the ahead reduction off).
+        uint64_t lagFor(DeviceProps const* props, int residentPerSm)
+        {
+            static long long const env = [] {
+                char const* e = getenv("A3B_SCAN_LAG");
+                return e ? atoll(e) : -1ll;
+            }();
+            if(env >= 0)
+                return static_cast<uint64_t>(env);
+            return 2ull * static_cast<uint64_t>(props->smCount) * static_cast<uint64_t>(residentPerSm);
+        }
+
+        template<typename T, bool INCL, bool VEC>
+        int launchScan(
+            cudaStream_t s,
+            DeviceProps const* props,
+            T const* in,
+            T* out,
+            uint64_t n,
+            uint64_t tiles,
+            int overlap,
+            T const* carry,
+            ScanHeader* hdr,
+            unsigned epoch,
+            uint64_t stallTile)
+        {
+            int resident = 0;
+            int rc = kernelResident<T, INCL, VEC>(props, &resident);
+            if(rc)
+                return rc;
+            uint64_t const lag = lagFor(props, resident);
+            int const dyn = VEC ? Traits<T>::STAGE : 0;
+            scanTileKernel<T, INCL, VEC><<<dim3(static_cast<unsigned>(tiles)), kBlock, dyn, s>>>(
+                in, out, n, tiles, lag, overlap, carry, hdr, epoch, props->errWord, waitTimeoutNs(), stallTile);
+            A3B_CHECK_LAUNCH("scan launch");
+            return A3B_OK;
         }
 
         template<typename T>
@@ -447,28 +862,17 @@ namespace a3b
                     return rc;
             }
             auto* hdr = static_cast<ScanHeader*>(scr);
-            uint64_t const to = waitTimeoutNs();
-            bool const vec = aligned16(in) && aligned16(out);
-            dim3 const grid(static_cast<unsigned>(tiles));
-#define A3B_SCAN_LAUNCH(INCL, VEC)                                                                                    \
-    scanTileKernel<T, INCL, VEC><<<grid, kBlock, 0, s>>>(in, out, n, carry, hdr, epoch, props->errWord, to, stallTile)
+            auto const packAligned = [](void const* p) {
+                return (reinterpret_cast<uintptr_t>(p) % static_cast<uintptr_t>(Traits<T>::PB)) == 0u;
+            };
+            bool const vec = packAligned(in) && packAligned(out);
+            auto const ib = reinterpret_cast<uintptr_t>(in), ob = reinterpret_cast<uintptr_t>(out);
+            int const overlap = (ib < ob + n * sizeof(T) && ob < ib + n * sizeof(T)) ? 1 : 0;
             if(inclusive)
-            {
-                if(vec)
-                    A3B_SCAN_LAUNCH(true, true);
-                else
-                    A3B_SCAN_LAUNCH(true, false);
-            }
-            else
-            {
-                if(vec)
-                    A3B_SCAN_LAUNCH(false, true);
-                else
-                    A3B_SCAN_LAUNCH(false, false);
-            }
-#undef A3B_SCAN_LAUNCH
-            A3B_CHECK_LAUNCH("scan launch");
-            return A3B_OK;
+                return vec ? launchScan<T, true, true>(s, props, in, out, n, tiles, overlap, carry, hdr, epoch, stallTile)
+                           : launchScan<T, true, false>(s, props, in, out, n, tiles, overlap, carry, hdr, epoch, stallTile);
+            return vec ? launchScan<T, false, true>(s, props, in, out, n, tiles, overlap, carry, hdr, epoch, stallTile)
+                       : launchScan<T, false, false>(s, props, in, out, n, tiles, overlap, carry, hdr, epoch, stallTile);
         }
 
         int scanEntry(
