@@ -219,7 +219,8 @@ A3B_API int a3b_reduce_lower_ranks(a3b_stream_t stream, a3b_peer_group* group, i
 A3B_API size_t a3b_scan_buffer_size(int dtype, uint64_t n);
 
 /* onHost::inclusiveScan / exclusiveScan / *InPlace (include/alpaka/onHost/algo/scan.hpp:45-218), operator +,
- * exclusive identity 0. One launch (single-pass decoupled look-back). in == out is allowed (in-place).
+ * exclusive identity 0. One cooperative launch of one block per SM that reads every element from HBM once and writes
+ * it once (tile aggregates published two rounds ahead of the tiles' scans). in == out is allowed (in-place).
  * buffer: optional caller scratch of at least a3b_scan_buffer_size bytes (any contents; it is cleared on the
  *         stream); null uses a scratch cached by the library per (device, stream).
  * carry_in: optional DEVICE pointer to one element added to every output (the sum of all preceding shards when a
@@ -227,8 +228,8 @@ A3B_API size_t a3b_scan_buffer_size(int dtype, uint64_t n);
 A3B_API int a3b_scan(a3b_stream_t stream, int dtype, int inclusive, void const* in, void* out, uint64_t n,
              void const* carry_in, void* buffer, size_t buffer_bytes);
 
-/* Failure-detection test hook: runs a3b_scan (no caller buffer) with tile `stall_tile` never publishing its status,
- * so every later tile's bounded look-back gives up after the configured timeout, raises bit 0 of the device error
+/* Failure-detection test hook: runs a3b_scan (no caller buffer) with tile `stall_tile` never publishing its aggregate,
+ * so every later tile's bounded wait for it gives up after the configured timeout, raises bit 0 of the device error
  * word and returns. The output is undefined; the context stays usable. */
 A3B_API int a3b_scan_debug_stall(a3b_stream_t stream, int dtype, void const* in, void* out, uint64_t n, uint64_t stall_tile);
 

@@ -38,13 +38,13 @@ def test_version_and_scan_buffer_size():
     from alpaka3_b200 import capi
     L = capi.lib()
     assert L.a3b_version() == 100
-    # 64-byte header + two status arrays (tile aggregates, inclusive prefixes), each one 8-byte word per 32 value bits
-    # per tile (16384 x 4-byte or 8192 x 8-byte elements per tile) rounded up to 256 bytes
-    tiles32 = -(-(1 << 30) // 16384)
-    assert L.a3b_scan_buffer_size(capi.U32, 1 << 30) == 64 + 2 * (-(-tiles32 * 8 // 256) * 256)
-    tiles64 = -(-(1 << 28) // 8192)
-    assert L.a3b_scan_buffer_size(capi.U64, 1 << 28) == 64 + 2 * (-(-tiles64 * 16 // 256) * 256)
-    assert L.a3b_scan_buffer_size(capi.U32, 1) == 64 + 2 * 256
+    # 64-byte header + one 8-byte status word per 32 value bits per 36 KB tile (9216 x 4-byte or 4608 x 8-byte
+    # elements), rounded up to 256 bytes
+    tiles32 = -(-(1 << 30) // 9216)
+    assert L.a3b_scan_buffer_size(capi.U32, 1 << 30) == 64 + -(-tiles32 * 8 // 256) * 256
+    tiles64 = -(-(1 << 28) // 4608)
+    assert L.a3b_scan_buffer_size(capi.U64, 1 << 28) == 64 + -(-tiles64 * 16 // 256) * 256
+    assert L.a3b_scan_buffer_size(capi.U32, 1) == 64 + 256
     assert L.a3b_scan_buffer_size(99, 10) == 0
 
 

@@ -1,5 +1,5 @@
 """GPU parity: single-pass scan against the reference's own pins (test/unit/algorithm/scan.cpp:74-197) and the
-oracle, bit-exact for integers; bounded look-back timeout (failure detection without a GPU fault)."""
+oracle, bit-exact for integers; bounded wait timeout (failure detection without a GPU fault)."""
 import hashlib
 import json
 import os
@@ -114,9 +114,9 @@ def test_repeated_calls_epochs(cuda, port):
     assert (_h(out2) == port.scan(_h(y), False)).all() and (_h(out) == want).all()
 
 
-def test_lookback_timeout_reports_error(cuda):
-    """A tile that never publishes (host-requested stall) makes its successors' bounded waits give up: the device
-    error word reports a timeout, the kernel returns, and the context keeps working."""
+def test_aggregate_wait_timeout_reports_error(cuda):
+    """A tile whose aggregate is never published (host-requested stall) makes the bounded waits of the tiles after it
+    give up: the device error word reports a timeout, the kernel returns, and the context keeps working."""
     import ctypes
     from alpaka3_b200 import algo, capi
     s = algo.stream_handle()
