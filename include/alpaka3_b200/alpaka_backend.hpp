@@ -4,6 +4,7 @@
  *   alpaka::onHost::transformReduce   (alpaka3: include/alpaka/onHost/algo/transformReduce.hpp:59-114)
  *   alpaka::onHost::reduce            (include/alpaka/onHost/algo/reduce.hpp:28-79)
  *   alpaka::onHost::exclusiveScan / inclusiveScan / *InPlace   (include/alpaka/onHost/algo/scan.hpp:45-218)
+ *   alpaka::onHost::transform         (include/alpaka/onHost/algo/transform.hpp:50-88; nvcc translation units only)
  * for queues of CUDA devices (Queue<Device<api::Cuda, K>, Q>). Partial ordering picks them over alpaka3's generic
  * templates because their queue parameter is more specialised. At run time a call goes to the C ABI when
  *   - the element type is int32/uint32/int64/uint64/float/double,
@@ -11,6 +12,9 @@
  *   - the reduce functor is std::plus or (probed on the host) computes +, min or max, and the transform functor is
  *     std::identity or computes x, x*x or a*b (probed with scalars, or with Simd<T, 1> for functors such as
  *     BabelStream's DotMultiplication that take SIMD packs);
+ * transform with any functor that takes alpaka::Simd packs (or a ScalarFunc taking scalars) and no accelerator, on
+ * device buffers of equal extents laid out densely or as pitched rows, runs the B200 element-wise engine of
+ * elementwise.cuh, compiled here by nvcc with the caller's functor;
  * every other call is forwarded unchanged to alpaka3's own implementation (onHost::internal::transformReduce /
  * internal::scan), so the caller's results never depend on the routing. Backend errors throw std::runtime_error, as
  * alpaka3's ALPAKA_UNIFORM_CUDA_HIP_RT_CHECK does (include/alpaka/core/UniformCudaHip.hpp:42). Blocking queues wait
@@ -21,6 +25,9 @@
 #include <alpaka/alpaka.hpp>
 
 #include "../alpaka3_b200.h"
+#if defined(__CUDACC__)
+#    include "elementwise.cuh"
+#endif
 
 #include <atomic>
 #include <cstdint>
@@ -29,6 +36,7 @@
 #include <stdexcept>
 #include <string>
 #include <type_traits>
+#include <utility>
 
 namespace alpaka3_b200
 {
@@ -306,6 +314,128 @@ namespace alpaka3_b200
             }
         }
 
+#if defined(__CUDACC__)
+        template<typename T, int V>
+        __device__ __forceinline__ auto toSimd(elementwise::Vec<T, V> const& x)
+        {
+            return alpaka::Simd<T, static_cast<std::uint32_t>(V)>([&](auto i) { return x.v[i]; });
+        }
+
+        //! Calls an alpaka3 functor with alpaka::Simd packs, as alpaka3's SimdTransformKernel does.
+        template<typename Fn, typename TOut, typename... TIn>
+        struct SimdOp
+        {
+            Fn fn;
+
+            template<int V>
+            __device__ __forceinline__ void apply(
+                elementwise::Vec<TOut, V>& out,
+                elementwise::Vec<TIn, V> const&... in) const
+            {
+                auto const r = fn(toSimd(in)...);
+#    pragma unroll
+                for(int k = 0; k < V; ++k)
+                    out.v[k] = static_cast<TOut>(r[k]);
+            }
+        };
+
+        template<typename F, typename TOut, std::uint32_t V, typename... TIn>
+        concept SimdCallable = requires(F const& f, alpaka::Simd<TIn, V> const&... s) {
+            { f(s...)[0u] } -> std::convertible_to<TOut>;
+        };
+
+        template<typename F, typename TOut, typename... TIn>
+        concept ScalarCallable = requires(F const& f, TIn const&... a) {
+            { f(a...) } -> std::convertible_to<TOut>;
+        };
+
+        //! 1: call with SIMD packs, 2: call with scalars (ScalarFunc), 0: not covered (stencil or accelerator functors)
+        template<typename F, typename TOut, typename... TIn>
+        constexpr int transformKind()
+        {
+            constexpr std::uint32_t W = static_cast<std::uint32_t>(elementwise::packWidth<TOut, TIn...>());
+            if constexpr(!std::is_arithmetic_v<TOut> || !(std::is_arithmetic_v<TIn> && ...))
+                return 0;
+            else if constexpr(alpaka::isSpecializationOf_v<F, alpaka::StencilFunc>)
+                return 0;
+            else if constexpr(alpaka::isSpecializationOf_v<F, alpaka::ScalarFunc>)
+                return ScalarCallable<F, TOut, TIn...> ? 2 : 0;
+            else if constexpr(SimdCallable<F, TOut, W, TIn...> && SimdCallable<F, TOut, 1u, TIn...>)
+                return 1;
+            else
+                return 0;
+        }
+
+        template<typename T>
+        elementwise::Rows<T> rowsOf(Layout const& l, bool dense)
+        {
+            auto* p = static_cast<T*>(const_cast<void*>(l.ptr));
+            return {p, dense ? 0u : (l.rowPitch != 0u ? l.rowPitch : l.rowLen * sizeof(std::remove_const_t<T>))};
+        }
+
+        template<typename A>
+        using ElemOf = std::remove_const_t<alpaka::trait::GetValueType_t<std::decay_t<A>>>;
+
+        // Run transform on the element-wise engine; false when the call is not covered.
+        template<typename Q, typename Out, typename Fn, typename... In>
+        bool tryTransform(Q const& queue, Out& out, Fn const& fn, In const&... in)
+        {
+            using TOut = ElemOf<Out>;
+            using F = std::decay_t<Fn>;
+            constexpr int NIN = sizeof...(In);
+            if constexpr(NIN < 1 || !(alpaka::concepts::IMdSpan<std::decay_t<In>> && ...))
+                return false;
+            else
+            {
+                constexpr int kind = transformKind<F, TOut, ElemOf<In>...>();
+                if constexpr(kind == 0)
+                    return false;
+                else
+                {
+                    auto const ext = alpaka::onHost::getExtents(out);
+                    if(((alpaka::onHost::getExtents(in) != ext) || ...))
+                        return false;
+                    Layout lo;
+                    Layout li[NIN];
+                    if(!layoutOf<TOut>(out, lo))
+                        return false;
+                    int k = 0;
+                    bool ok = true;
+                    ((ok = ok && layoutOf<ElemOf<In>>(in, li[k++])), ...); // a fold over "," runs left to right
+                    if(!ok)
+                        return false;
+                    bool dense = lo.dense();
+                    for(int j = 0; j < NIN; ++j)
+                        dense = dense && li[j].dense();
+                    std::uint64_t const rows = dense ? 1u : lo.rows;
+                    std::uint64_t const rowLen = dense ? lo.rows * lo.rowLen : lo.rowLen;
+                    auto const s = static_cast<cudaStream_t>(streamOf(queue));
+                    using Op = std::conditional_t<
+                        kind == 1,
+                        SimdOp<F, TOut, ElemOf<In>...>,
+                        elementwise::ScalarOp<F, TOut, ElemOf<In>...>>;
+                    cudaError_t const e = [&]<std::size_t... I>(std::index_sequence<I...>)
+                    {
+                        return elementwise::launch(
+                            s,
+                            rowsOf<TOut>(lo, dense),
+                            rows,
+                            rowLen,
+                            Op{fn},
+                            rowsOf<ElemOf<In> const>(li[I], dense)...);
+                    }(std::index_sequence_for<In...>{});
+                    if(e == cudaErrorInvalidValue)
+                        return false; // more chunks than one launch takes
+                    if(e != cudaSuccess)
+                        throw std::runtime_error(std::string("alpaka3_b200 transform: ") + cudaGetErrorString(e));
+                    finish(queue);
+                    ++routingStats().routed;
+                    return true;
+                }
+            }
+        }
+#endif
+
         template<typename Q>
         auto resolveExec(Q const& queue, auto exec)
         {
@@ -471,4 +601,40 @@ namespace alpaka::onHost
     ALPAKA3_B200_SCAN_OVERLOADS(exclusiveScan, false, EXCLUSIVE_SCAN)
     ALPAKA3_B200_SCAN_OVERLOADS(inclusiveScan, true, INCLUSIVE_SCAN)
 #undef ALPAKA3_B200_SCAN_OVERLOADS
+    // ------------------------------------------------------------------------------------------------ transform
+    template<alpaka::concepts::DeviceKind T_DeviceKind, alpaka::concepts::QueueKind T_QueueKind>
+    inline void transform(
+        Queue<Device<api::Cuda, T_DeviceKind>, T_QueueKind> const& queue,
+        alpaka::concepts::Executor auto const exec,
+        alpaka::concepts::IMdSpan auto&& out,
+        auto&& fn,
+        alpaka::concepts::IDataSource auto&&... in)
+    {
+#if defined(__CUDACC__)
+        if(alpaka3_b200::detail::tryTransform(queue, out, fn, in...))
+            return;
+#endif
+        ++alpaka3_b200::routingStats().forwarded;
+        internal::transform(
+            queue,
+            alpaka3_b200::detail::resolveExec(queue, exec),
+            ALPAKA_FORWARD(out),
+            ALPAKA_FORWARD(fn),
+            ALPAKA_FORWARD(in)...);
+    }
+
+    template<alpaka::concepts::DeviceKind T_DeviceKind, alpaka::concepts::QueueKind T_QueueKind>
+    inline void transform(
+        Queue<Device<api::Cuda, T_DeviceKind>, T_QueueKind> const& queue,
+        alpaka::concepts::IMdSpan auto&& out,
+        auto&& fn,
+        alpaka::concepts::IDataSource auto&&... in)
+    {
+        transform(
+            queue,
+            defaultExecutor(queue.getDevice()),
+            ALPAKA_FORWARD(out),
+            ALPAKA_FORWARD(fn),
+            ALPAKA_FORWARD(in)...);
+    }
 } // namespace alpaka::onHost

@@ -3,7 +3,10 @@
  * backend. Mirrors test/unit/algorithm/scan.cpp:74-197 (int iota, 4 sizes, exclusive/inclusive x out-of-place /
  * in-place x with/without buffer, std::exclusive_scan / std::inclusive_scan as ground truth) and
  * test/unit/algorithm/reduce.cpp:135-232 (int iota over N-D extents, plus / min / max, plus the generator source),
- * plus BabelStream's dot (benchmark/babelstream/src/babelStreamMainTest.cpp:135-141, 337-345).
+ * plus BabelStream's dot (benchmark/babelstream/src/babelStreamMainTest.cpp:135-141, 337-345), and
+ * test/unit/algorithm/transform.cpp:147-180 (int inputs over the same N-D extents with std::minus, std::plus, a
+ * StencilFunc, ScalarFunc with and without an accelerator argument, and an up-casting functor), plus an in-place
+ * transform of a large 1-D float array with a ragged end.
  * Prints one line "PASS routed=<n> forwarded=<m>" and exits 0, or lists the failures and exits 1. */
 #include <alpaka3_b200/alpaka_backend.hpp>
 
@@ -127,6 +130,135 @@ namespace
         }
     }
 
+    // functors of test/unit/algorithm/transform.cpp
+    struct StencilAdd
+    {
+        constexpr auto operator()(concepts::SimdPtr auto const& a, concepts::SimdPtr auto const& b) const
+        {
+            return a.load() + b.load();
+        }
+    };
+
+    struct ScalarMinPlusOne
+    {
+        constexpr auto operator()(int const& a, int const& b) const
+        {
+            return math::min(a + 1, b);
+        }
+    };
+
+    struct ScalarOpWithAcc
+    {
+        constexpr auto operator()(onAcc::concepts::Acc auto const&, auto const& a, auto const& b) const
+        {
+            using ValueType = trait::GetValueType_t<ALPAKA_TYPEOF(a)>;
+            return math::min(a + ValueType{1}, +b);
+        }
+    };
+
+    struct AddUpCast
+    {
+        constexpr auto operator()(concepts::Simd auto const& a, concepts::Simd auto const& b) const
+        {
+            return pCast<std::size_t>(a + b);
+        }
+    };
+
+    struct AddUpCastWithAcc
+    {
+        constexpr auto operator()(
+            onAcc::concepts::Acc auto const&,
+            concepts::Simd auto const& a,
+            concepts::Simd auto const& b) const
+        {
+            return pCast<std::size_t>(a + b);
+        }
+    };
+
+    //! out = fn(a, b) with a[i] = i, b[i] = 3 - 2 i over `extents`; checks every element against `want` and whether
+    //! the call ran on the element-wise engine (routed) or on alpaka3's own backend (forwarded).
+    template<typename TOut>
+    void transformOne(auto& dev, auto& queue, auto exec, auto extents, auto fn, auto want, bool routed, char const* what)
+    {
+        using T = int;
+        auto a = onHost::alloc<T>(dev, extents);
+        auto b = onHost::allocLike(dev, a);
+        auto ha = onHost::allocHostLike(a);
+        auto hb = onHost::allocHostLike(b);
+        T c = 0;
+        for(auto& v : ha)
+            v = c++;
+        c = 0;
+        for(auto& v : hb)
+            v = 3 - 2 * c++;
+        onHost::memcpy(queue, a, ha);
+        onHost::memcpy(queue, b, hb);
+        auto out = onHost::alloc<TOut>(dev, extents);
+        auto ho = onHost::allocHostLike(out);
+        auto const before = alpaka3_b200::routingStats().routed.load();
+        onHost::transform(queue, exec, out, fn, a, b);
+        onHost::memcpy(queue, ho, out);
+        onHost::wait(queue);
+        expect((alpaka3_b200::routingStats().routed.load() != before) == routed, what, routed ? 1 : 0, 0);
+        long long i = 0;
+        int bad = 0;
+        for(auto const& v : ho)
+        {
+            T const x = static_cast<T>(i), y = static_cast<T>(3 - 2 * i);
+            if(v != static_cast<TOut>(want(x, y)) && bad++ < 3)
+                expect(false, what, static_cast<long long>(v), static_cast<long long>(want(x, y)));
+            ++i;
+        }
+    }
+
+    void transformTests(auto& dev, auto& queue, auto exec, auto extents)
+    {
+        auto minus = [](int x, int y) { return x - y; };
+        auto plus = [](int x, int y) { return x + y; };
+        auto minPlusOne = [](int x, int y) { return std::min(x + 1, y); };
+        transformOne<int>(dev, queue, exec, extents, std::minus{}, minus, true, "transform minus");
+        transformOne<int>(dev, queue, exec, extents, std::plus{}, plus, true, "transform plus");
+        transformOne<int>(dev, queue, exec, extents, StencilFunc{StencilAdd{}}, plus, false, "transform stencil");
+        transformOne<int>(dev, queue, exec, extents, ScalarFunc{ScalarMinPlusOne{}}, minPlusOne, true, "transform scalar");
+        transformOne<int>(dev, queue, exec, extents, ScalarFunc{ScalarOpWithAcc{}}, minPlusOne, false, "transform scalar acc");
+        transformOne<std::size_t>(dev, queue, exec, extents, AddUpCast{}, plus, true, "transform up-cast");
+        transformOne<std::size_t>(dev, queue, exec, extents, AddUpCastWithAcc{}, plus, false, "transform up-cast acc");
+    }
+
+    struct TwiceAndOne
+    {
+        constexpr auto operator()(auto const& x) const
+        {
+            return x * 2.f + 1.f;
+        }
+    };
+
+    //! the element-wise engine on a large 1-D array with a ragged end, in place
+    void transformLarge(auto& dev, auto& queue, auto exec)
+    {
+        std::size_t const n = (std::size_t{1} << 22) + 5;
+        auto a = onHost::alloc<float>(dev, Vec{n});
+        auto ha = onHost::allocHostLike(a);
+        float c = 0.f;
+        for(auto& v : ha)
+            v = c++ * 0.25f;
+        onHost::memcpy(queue, a, ha);
+        auto const before = alpaka3_b200::routingStats().routed.load();
+        onHost::transform(queue, exec, a, TwiceAndOne{}, a);
+        auto h2 = onHost::allocHostLike(a);
+        onHost::memcpy(queue, h2, a);
+        onHost::wait(queue);
+        expect(alpaka3_b200::routingStats().routed.load() == before + 1, "transform large routed");
+        std::size_t i = 0, bad = 0;
+        for(auto const& v : h2)
+        {
+            float const want = (static_cast<float>(i) * 0.25f) * 2.f + 1.f;
+            if(v != want && bad++ < 3)
+                expect(false, "transform large", static_cast<long long>(v), static_cast<long long>(want));
+            ++i;
+        }
+    }
+
     template<typename T>
     T hostReduce(int op, std::size_t n, T init)
     {
@@ -216,6 +348,14 @@ int main()
     reduceOne(dev, queue, exec, Vec{7, 3});
     reduceOne(dev, queue, exec, Vec{3});
     transformReduceTests(dev, queue, exec);
+    // extents of test/unit/algorithm/transform.cpp:177-178
+    transformTests(dev, queue, exec, Vec{5, 7, 3, 11});
+    transformTests(dev, queue, exec, Vec{93, 7, 123});
+    transformTests(dev, queue, exec, Vec{5, 7, 4111});
+    transformTests(dev, queue, exec, Vec{5, 7, 3});
+    transformTests(dev, queue, exec, Vec{7, 3});
+    transformTests(dev, queue, exec, Vec{3});
+    transformLarge(dev, queue, exec);
     auto& st = alpaka3_b200::routingStats();
     if(failures == 0)
         std::printf("PASS routed=%llu forwarded=%llu\n", static_cast<unsigned long long>(st.routed.load()),

@@ -1,5 +1,6 @@
-"""GPU: alpaka3's own algorithm tests (scan.cpp / reduce.cpp pins, BabelStream dot) through alpaka3's public onHost API
-on a CUDA queue with the alpaka3_b200 binding: covered calls go to the C ABI, the others to alpaka3's CUDA backend."""
+"""GPU: alpaka3's own algorithm tests (scan.cpp / reduce.cpp / transform.cpp pins, BabelStream dot) through alpaka3's
+public onHost API on a CUDA queue with the alpaka3_b200 binding: covered calls go to the C ABI or the element-wise
+engine, the others to alpaka3's CUDA backend."""
 import os
 import re
 import subprocess
@@ -19,7 +20,9 @@ def test_alpaka_api_through_binding(cuda):
     m = re.search(r"PASS routed=(\d+) forwarded=(\d+)", p.stdout)
     assert m, p.stdout
     routed, forwarded = int(m.group(1)), int(m.group(2))
-    # 4 sizes x 8 scan variants + 6 extents x 3 reduce ops + the dot are routed; generator sources and the
-    # unrecognised transform stay on alpaka3's own backend
-    assert routed >= 4 * 8 + 6 * 3 + 1, p.stdout
-    assert forwarded >= 6 + 1, p.stdout
+    # routed: 4 sizes x 8 scan variants, 6 extents x 3 reduce ops, the dot, 6 extents x 4 transforms (std::minus,
+    # std::plus, ScalarFunc, up-cast) and the large in-place transform; forwarded to alpaka3's own backend: the 6
+    # generator reductions, the unrecognised transformReduce and 6 extents x 3 transforms (StencilFunc and the two
+    # functors that take an accelerator)
+    assert routed >= 4 * 8 + 6 * 3 + 1 + 6 * 4 + 1, p.stdout
+    assert forwarded >= 6 + 1 + 6 * 3, p.stdout
