@@ -135,3 +135,68 @@ def test_aggregate_wait_timeout_reports_error(cuda):
     algo.exclusive_scan(out, x)
     assert (_h(out) == np.arange(n)).all()
     assert capi.device_error(s, clear=True) == 0
+
+
+# The scan runs one block per SM (G = 148 on B200) over 36 KB tiles (9216 x 4-byte, 4608 x 8-byte elements) in rounds;
+# a tile's aggregate is taken two rounds before its scan. These sizes sit on the edges of that structure: one tile,
+# G tiles, G tiles + 1 element, more than the two-round lag, and ragged last tiles.
+_G = 148
+
+
+def _edge_sizes(tile):
+    return [tile - 1, tile, tile + 1, _G * tile, _G * tile + 1, 3 * _G * tile + 7, 5 * _G * tile - 3]
+
+
+@pytest.mark.parametrize("dtype,tile", [(torch.int32, 9216), (torch.int64, 4608)])
+def test_scan_round_structure_sizes(cuda, port, dtype, tile):
+    from alpaka3_b200 import algo
+    from oracle.oracle import SEED
+    for n in _edge_sizes(tile):
+        if dtype == torch.int32:
+            x = torch.empty(n, dtype=torch.int32, device=cuda)
+            algo.random_u32(x, SEED, shift=28)
+        else:
+            x = torch.empty(n, dtype=torch.int64, device=cuda)
+            algo.random_u64(x, SEED)
+        h = _h(x)
+        out = torch.empty_like(x)
+        for incl in (False, True):
+            (algo.inclusive_scan if incl else algo.exclusive_scan)(out, x)
+            assert (_h(out) == port.scan(h, incl)).all(), (n, incl)
+
+
+def test_scan_in_place_with_exact_buffer_multi_round(cuda, port):
+    """in place over several rounds with a ragged last tile, scratch in a caller buffer of exactly
+    a3b_scan_buffer_size bytes"""
+    from alpaka3_b200 import algo
+    n = 4 * _G * 9216 + 4097
+    x = torch.randint(-1000, 1000, (n,), dtype=torch.int32, device=cuda)
+    want = port.scan(_h(x), True)
+    buf = torch.empty(algo.get_scan_buffer_size(torch.int32, n), dtype=torch.uint8, device=cuda)
+    algo.inclusive_scan_in_place(x, buffer=buf)
+    assert (_h(x) == want).all()
+
+
+def test_scan_unaligned_multi_round(cuda, port):
+    """4-byte offset input and output (no 16-byte packs, no TMA) over several rounds, with a carry"""
+    from alpaka3_b200 import algo
+    n = 3 * _G * 9216 + 11
+    base = torch.randint(0, 16, (n + 1,), dtype=torch.int32, device=cuda)
+    x = base[1:]
+    out = torch.empty(n + 3, dtype=torch.int32, device=cuda)[3:]
+    carry = torch.tensor([-5], dtype=torch.int32, device=cuda)
+    algo.exclusive_scan(out, x, carry=carry)
+    assert (_h(out) == port.scan(_h(x), False) - 5).all()
+
+
+def test_float_scan_is_deterministic(cuda):
+    """tile aggregates are combined in a fixed order, so repeated floating-point scans give identical bits"""
+    from alpaka3_b200 import algo
+    for dtype in (torch.float32, torch.float64):
+        x = torch.rand(2 * _G * 9216 + 333, dtype=dtype, device=cuda) - 0.5
+        a = torch.empty_like(x)
+        b = torch.empty_like(x)
+        algo.inclusive_scan(a, x)
+        for _ in range(3):
+            algo.inclusive_scan(b, x)
+            assert torch.equal(a, b)
