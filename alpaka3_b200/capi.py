@@ -69,9 +69,15 @@ SIGNATURES = {
     "a3b_heat_step": [_P, _P, _P, _U64, _U64, _U64, _U64, _U64, _D, _D],
     "a3b_heat_init": [_P, _P, _U64, _U64, _U64, _U64, _U64, _D, _D],
     "a3b_heat_exact": [_P, _P, _U64, _U64, _U64, _U64, _U64, _D, _D, _D, _I],
+    "a3b_halo_bytes": [_U64],
+    "a3b_halo_create": [_I, _I, _U64, _P, _P],
+    "a3b_halo_connect": [_P, _P],
+    "a3b_halo_destroy": [_P],
+    "a3b_heat_halo_publish": [_P, _P, _P, _U64, _U64, _U64],
+    "a3b_heat_step_halo": [_P, _P, _P, _P, _U64, _U64, _U64, _D, _D],
 }
 _RESTYPES = {"a3b_last_error": ctypes.c_char_p, "a3b_scan_buffer_size": ctypes.c_size_t,
-             "a3b_ipc_handle_size": ctypes.c_size_t}
+             "a3b_ipc_handle_size": ctypes.c_size_t, "a3b_halo_bytes": ctypes.c_size_t}
 
 
 class LibraryNotBuilt(RuntimeError):

@@ -10,6 +10,8 @@
 //   next = c*(1 - 2rX - 2rY) + w*rX + e*rX + n*rY + s*rY
 #include <math_constants.h>
 
+#include <cstring>
+
 #include "common.cuh"
 
 namespace a3b
@@ -31,24 +33,25 @@ namespace a3b
             return v;
         }
 
-        // storage columns (c0, c0 + 1) with c0 = 2 * (global thread x); rows [rb, re) of the interior band
-        __global__ void __launch_bounds__(kThreads) heatKernelVec(
+        // One band of rows [rb, re) for the thread's storage columns (c0, c0 + 1), c0 = 2 * (global thread x). Ghost
+        // rows 0 and rows + 1 come from `north` / `south` when those are set (a neighbour's boundary row in this rank's
+        // halo mailbox, read past L1), otherwise from `cur` like every other row.
+        __device__ __forceinline__ void heatBand(
             double const* __restrict__ cur,
             double* __restrict__ next,
             uint64_t cols,
             uint64_t pitch,
-            uint64_t rowBegin,
-            uint64_t rowEnd,
+            uint64_t rb,
+            uint64_t re,
             double rX,
-            double rY)
+            double rY,
+            uint64_t rows,
+            double const* north,
+            double const* south)
         {
             int const lane = threadIdx.x & 31;
             uint64_t const width = cols + 2u; // storage columns
             uint64_t const c0 = 2u * (static_cast<uint64_t>(blockIdx.x) * kThreads + threadIdx.x);
-            uint64_t const rb = rowBegin + static_cast<uint64_t>(blockIdx.y) * kBand;
-            if(rb >= rowEnd)
-                return;
-            uint64_t const re = rb + kBand < rowEnd ? rb + kBand : rowEnd;
             bool const live = c0 < width;       // this thread's pack starts inside the row
             bool const hasHi = c0 + 1u < width; // and its second column exists
             uint64_t const cl = live ? c0 : 0u; // clamped load column (always a valid pack start)
@@ -56,6 +59,13 @@ namespace a3b
 
             auto ldPack = [&](uint64_t r) -> double2
             {
+                double const* ghost = (r == 0u) ? north : (r == rows + 1u ? south : nullptr);
+                if(ghost)
+                {
+                    if(hasHi)
+                        return __ldcg(reinterpret_cast<double2 const*>(ghost + cl));
+                    return make_double2(live ? __ldcg(ghost + cl) : 0.0, 0.0);
+                }
                 double const* p = cur + r * pitch + cl;
                 if(hasHi)
                     return __ldcs(reinterpret_cast<double2 const*>(p));
@@ -89,7 +99,7 @@ namespace a3b
 #pragma unroll
                 for(int a = 0; a < kAhead; ++a)
                 {
-                    double2 const south = dn[a];
+                    double2 const south2 = dn[a];
                     double westOfLo = __shfl_up_sync(0xffffffffu, mid.y, 1);
                     double eastOfHi = __shfl_down_sync(0xffffffffu, mid.x, 1);
                     if(lane == 0)
@@ -102,8 +112,8 @@ namespace a3b
                         double* const q = next + row * pitch + c0;
                         bool const loIn = c0 >= 1u && c0 <= cols;
                         bool const hiIn = hasHi && c0 + 1u <= cols;
-                        double const lo = cell(mid.x, westOfLo, mid.y, up.x, south.x, k, rX, rY);
-                        double const hi = cell(mid.y, mid.x, eastOfHi, up.y, south.y, k, rX, rY);
+                        double const lo = cell(mid.x, westOfLo, mid.y, up.x, south2.x, k, rX, rY);
+                        double const hi = cell(mid.y, mid.x, eastOfHi, up.y, south2.y, k, rX, rY);
                         if(loIn && hiIn)
                             __stcs(reinterpret_cast<double2*>(q), make_double2(lo, hi));
                         else
@@ -115,9 +125,187 @@ namespace a3b
                         }
                     }
                     up = mid;
-                    mid = south;
+                    mid = south2;
                 }
             }
+        }
+
+        // rows [rowBegin, rowEnd) of the interior, one band of kBand rows per blockIdx.y
+        __global__ void __launch_bounds__(kThreads) heatKernelVec(
+            double const* __restrict__ cur,
+            double* __restrict__ next,
+            uint64_t cols,
+            uint64_t pitch,
+            uint64_t rowBegin,
+            uint64_t rowEnd,
+            double rX,
+            double rY)
+        {
+            uint64_t const rb = rowBegin + static_cast<uint64_t>(blockIdx.y) * kBand;
+            if(rb >= rowEnd)
+                return;
+            uint64_t const re = rb + kBand < rowEnd ? rb + kBand : rowEnd;
+            heatBand(cur, next, cols, pitch, rb, re, rX, rY, ~uint64_t{0} - 1u, nullptr, nullptr);
+        }
+
+        // ------------------------------------------------------------------------ step fused with the halo exchange
+        // Halo mailbox of one rank (cudaMalloc, mapped by its neighbours through CUDA IPC):
+        //   u32  flag[2 sides][2 parities][kMaxColBlocks]   step number (+1) whose row slice column block x has written
+        //   f64  row[2 sides][2 parities][cols + 2]         a neighbour's boundary row (storage columns)
+        // side 0 holds the upper neighbour's last interior row (this rank's north ghost), side 1 the lower neighbour's
+        // first interior row (south ghost). Step s reads parity (s - 1) & 1 and writes parity s & 1 of its neighbours.
+        constexpr unsigned kMaxColBlocks = 1024; // columns up to 2 * 256 * 1024 - 2
+        constexpr uint64_t kFlagBytes = 2u * 2u * kMaxColBlocks * sizeof(unsigned);
+
+        __host__ __device__ inline uint64_t mailRowStride(uint64_t cols)
+        {
+            return ((cols + 2u) + 31u) & ~uint64_t{31u}; // doubles, 256-byte multiple
+        }
+
+        __host__ __device__ inline uint64_t mailBytes(uint64_t cols)
+        {
+            return kFlagBytes + 4u * mailRowStride(cols) * sizeof(double);
+        }
+
+        struct Mail
+        {
+            unsigned* flags;
+            double* rows;
+            uint64_t stride;
+
+            __device__ unsigned* flag(int side, unsigned parity, unsigned x) const
+            {
+                return flags + (static_cast<unsigned>(side) * 2u + parity) * kMaxColBlocks + x;
+            }
+
+            __device__ double* row(int side, unsigned parity) const
+            {
+                return rows + (static_cast<uint64_t>(side) * 2u + parity) * stride;
+            }
+        };
+
+        __device__ __forceinline__ unsigned ldAcquireSys32(unsigned const* p)
+        {
+            unsigned v;
+            asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+            return v;
+        }
+
+        __device__ __forceinline__ void stReleaseSys32(unsigned* p, unsigned v)
+        {
+            asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+        }
+
+        // Thread 0 waits until flag >= want (bounded by %globaltimer); false (and the error word raised) on timeout.
+        __device__ bool waitFlag(unsigned const* flag, unsigned want, uint64_t timeoutNs, unsigned* errWord)
+        {
+            __shared__ int ok;
+            if(threadIdx.x == 0)
+            {
+                ok = 1;
+                uint64_t const t0 = globalTimerNs();
+                while(static_cast<int>(ldAcquireSys32(flag) - want) < 0)
+                {
+                    if(globalTimerNs() - t0 > timeoutNs)
+                    {
+                        atomicOr(errWord, kErrTimeout);
+                        ok = 0;
+                        break;
+                    }
+                    __nanosleep(128);
+                }
+            }
+            __syncthreads();
+            bool const r = ok != 0;
+            __syncthreads(); // every thread has read `ok` before a second wait of the block rewrites it
+            return r;
+        }
+
+        // This block's columns of `row` (storage row of `next`) into a neighbour's mailbox row, then the block's flag.
+        __device__ void sendRow(double const* row, uint64_t cols, double* dst, unsigned* flag, unsigned value)
+        {
+            uint64_t const width = cols + 2u;
+            uint64_t const c0 = 2u * (static_cast<uint64_t>(blockIdx.x) * kThreads + threadIdx.x);
+            if(c0 + 1u < width)
+                *reinterpret_cast<double2*>(dst + c0) = *reinterpret_cast<double2 const*>(row + c0);
+            else if(c0 < width)
+                dst[c0] = row[c0];
+            __threadfence_system(); // the row reaches the neighbour before the flag that announces it
+            __syncthreads();
+            if(threadIdx.x == 0)
+                stReleaseSys32(flag, value);
+        }
+
+        // One step of the slab: blockIdx.y = 0 is the first band, 1 the last band, the others the bands in between, so
+        // that both boundary rows are computed and sent first. The boundary bands wait for the neighbours' rows of the
+        // previous step; the interior bands never wait.
+        __global__ void __launch_bounds__(kThreads) heatExchangeKernel(
+            double const* __restrict__ cur,
+            double* __restrict__ next,
+            uint64_t rows,
+            uint64_t cols,
+            uint64_t pitch,
+            double rX,
+            double rY,
+            Mail mine,
+            Mail up,   // upper neighbour's mailbox (rows == nullptr: none, global boundary)
+            Mail down, // lower neighbour's mailbox
+            unsigned step,
+            uint64_t timeoutNs,
+            unsigned* errWord)
+        {
+            uint64_t const bands = (rows + kBand - 1u) / kBand;
+            uint64_t band = blockIdx.y;
+            if(bands > 1u)
+                band = blockIdx.y == 0u ? 0u : (blockIdx.y == 1u ? bands - 1u : blockIdx.y - 1u);
+            else if(blockIdx.y > 0u)
+                return;
+            uint64_t const rb = 1u + band * kBand;
+            uint64_t const re = rb + kBand < rows + 1u ? rb + kBand : rows + 1u;
+            bool const top = rb == 1u, bottom = re == rows + 1u;
+            unsigned const rd = (step - 1u) & 1u, wr = step & 1u;
+            double const* north = nullptr;
+            double const* south = nullptr;
+            if(top && up.rows)
+            {
+                if(!waitFlag(mine.flag(0, rd, blockIdx.x), step, timeoutNs, errWord))
+                    return;
+                north = mine.row(0, rd);
+            }
+            if(bottom && down.rows)
+            {
+                if(!waitFlag(mine.flag(1, rd, blockIdx.x), step, timeoutNs, errWord))
+                    return;
+                south = mine.row(1, rd);
+            }
+            heatBand(cur, next, cols, pitch, rb, re, rX, rY, rows, north, south);
+            if(top && up.rows)
+            {
+                __syncthreads(); // the block's row 1 is in `next`
+                sendRow(next + pitch, cols, up.row(1, wr), up.flag(1, wr, blockIdx.x), step + 1u);
+            }
+            if(bottom && down.rows)
+            {
+                __syncthreads();
+                sendRow(next + rows * pitch, cols, down.row(0, wr), down.flag(0, wr, blockIdx.x), step + 1u);
+            }
+        }
+
+        // Step-0 rows: this rank's first and last interior rows of the initial field into the neighbours' mailboxes.
+        __global__ void __launch_bounds__(kThreads) heatPublishKernel(
+            double const* __restrict__ u,
+            uint64_t rows,
+            uint64_t cols,
+            uint64_t pitch,
+            Mail up,
+            Mail down,
+            unsigned step)
+        {
+            unsigned const wr = step & 1u;
+            if(blockIdx.y == 0u && up.rows)
+                sendRow(u + pitch, cols, up.row(1, wr), up.flag(1, wr, blockIdx.x), step + 1u);
+            if(blockIdx.y == 1u && down.rows)
+                sendRow(u + rows * pitch, cols, down.row(0, wr), down.flag(0, wr, blockIdx.x), step + 1u);
         }
 
         // fallback for unaligned grids: one column per thread, plain loads
@@ -197,7 +385,47 @@ namespace a3b
     } // namespace
 } // namespace a3b
 
+// Halo mailbox of one rank and the mappings of its neighbours' mailboxes (CUDA IPC over NVLink).
+struct a3b_halo
+{
+    int device = -1;
+    int world = 0;
+    int rank = 0;
+    uint64_t cols = 0;
+    void* local = nullptr;
+    void* up = nullptr;   // mailbox of rank - 1
+    void* down = nullptr; // mailbox of rank + 1
+    unsigned step = 0;    // steps (and publications) issued so far, the same sequence on every rank
+    bool connected = false;
+};
+
 using namespace a3b;
+
+namespace
+{
+    Mail mailOf(void* base, uint64_t cols)
+    {
+        if(!base)
+            return Mail{nullptr, nullptr, 0u};
+        auto* b = static_cast<unsigned char*>(base);
+        return Mail{reinterpret_cast<unsigned*>(b), reinterpret_cast<double*>(b + kFlagBytes), mailRowStride(cols)};
+    }
+
+    int haloCheck(a3b_halo* h, double const* u, uint64_t rows, uint64_t cols, uint64_t pitch, unsigned* colBlocks)
+    {
+        A3B_REQUIRE(h && h->connected, "halo mailbox not connected");
+        A3B_REQUIRE(u, "null grid pointer");
+        A3B_REQUIRE(cols == h->cols, "grid columns differ from the mailbox's");
+        A3B_REQUIRE(rows >= 1u && pitch >= cols + 2u, "bad slab shape");
+        A3B_REQUIRE(aligned16(u) && pitch % 2u == 0u, "halo steps need 16-byte aligned rows (even pitch)");
+        int dev = -1;
+        A3B_CUDA(cudaGetDevice(&dev));
+        A3B_REQUIRE(dev == h->device, "halo mailbox used on a different device than the one it was created on");
+        uint64_t const packs = (cols + 2u + 1u) / 2u;
+        *colBlocks = static_cast<unsigned>((packs + kThreads - 1) / kThreads);
+        return A3B_OK;
+    }
+} // namespace
 
 extern "C"
 {
@@ -230,6 +458,119 @@ extern "C"
             heatKernelScalar<<<grid, kThreads, 0, s>>>(cur, next, cols, pitch_elems, row_begin, row_end, rX, rY);
         }
         A3B_CHECK_LAUNCH("heat step launch");
+        return A3B_OK;
+    }
+
+    size_t a3b_halo_bytes(uint64_t cols)
+    {
+        return static_cast<size_t>(mailBytes(cols));
+    }
+
+    int a3b_halo_create(int world, int rank, uint64_t cols, a3b_halo** halo, void* local_handle)
+    {
+        A3B_REQUIRE(halo && local_handle, "null argument");
+        A3B_REQUIRE(world >= 1 && rank >= 0 && rank < world, "world/rank out of range");
+        A3B_REQUIRE(cols >= 1u && (cols + 2u + 1u) / 2u <= static_cast<uint64_t>(kThreads) * kMaxColBlocks,
+                    "too many columns for the halo mailbox");
+        auto* h = new a3b_halo{};
+        h->world = world;
+        h->rank = rank;
+        h->cols = cols;
+        cudaError_t e = cudaGetDevice(&h->device);
+        if(e == cudaSuccess)
+            e = cudaMalloc(&h->local, mailBytes(cols));
+        if(e == cudaSuccess)
+            e = cudaMemset(h->local, 0, mailBytes(cols));
+        if(e == cudaSuccess)
+            e = cudaDeviceSynchronize(); // zeroed before a neighbour can write into it
+        cudaIpcMemHandle_t ih{};
+        if(e == cudaSuccess)
+            e = cudaIpcGetMemHandle(&ih, h->local);
+        if(e != cudaSuccess)
+        {
+            if(h->local)
+                cudaFree(h->local);
+            delete h;
+            return cudaFail(e, "a3b_halo_create");
+        }
+        std::memcpy(local_handle, &ih, sizeof(ih));
+        *halo = h;
+        return A3B_OK;
+    }
+
+    int a3b_halo_connect(a3b_halo* h, void const* handles)
+    {
+        A3B_REQUIRE(h && handles, "null argument");
+        A3B_REQUIRE(!h->connected, "halo mailbox already connected");
+        auto const* hs = static_cast<cudaIpcMemHandle_t const*>(handles);
+        cudaError_t e = cudaSuccess;
+        if(h->rank > 0)
+            e = cudaIpcOpenMemHandle(&h->up, hs[h->rank - 1], cudaIpcMemLazyEnablePeerAccess);
+        if(e == cudaSuccess && h->rank + 1 < h->world)
+            e = cudaIpcOpenMemHandle(&h->down, hs[h->rank + 1], cudaIpcMemLazyEnablePeerAccess);
+        if(e != cudaSuccess)
+        {
+            if(h->up)
+                cudaIpcCloseMemHandle(h->up);
+            h->up = nullptr;
+            return cudaFail(e, "cudaIpcOpenMemHandle (halo mailbox)");
+        }
+        h->connected = true;
+        return A3B_OK;
+    }
+
+    int a3b_halo_destroy(a3b_halo* h)
+    {
+        if(!h)
+            return A3B_OK;
+        int rc = A3B_OK;
+        if(h->up && cudaIpcCloseMemHandle(h->up) != cudaSuccess)
+            rc = A3B_ERR_CUDA;
+        if(h->down && cudaIpcCloseMemHandle(h->down) != cudaSuccess)
+            rc = A3B_ERR_CUDA;
+        if(h->local && cudaFree(h->local) != cudaSuccess)
+            rc = A3B_ERR_CUDA;
+        delete h;
+        if(rc)
+            setError("a3b_halo_destroy: releasing a mapping or the mailbox failed");
+        return rc;
+    }
+
+    int a3b_heat_halo_publish(a3b_stream_t stream, a3b_halo* h, double const* u, uint64_t rows, uint64_t cols,
+                              uint64_t pitch_elems)
+    {
+        unsigned colBlocks = 0;
+        int rc = haloCheck(h, u, rows, cols, pitch_elems, &colBlocks);
+        if(rc)
+            return rc;
+        unsigned const step = ++h->step;
+        dim3 const grid(colBlocks, 2u);
+        heatPublishKernel<<<grid, kThreads, 0, static_cast<cudaStream_t>(stream)>>>(
+            u, rows, cols, pitch_elems, mailOf(h->up, cols), mailOf(h->down, cols), step);
+        A3B_CHECK_LAUNCH("heat halo publish launch");
+        return A3B_OK;
+    }
+
+    int a3b_heat_step_halo(a3b_stream_t stream, a3b_halo* h, double const* cur, double* next, uint64_t rows,
+                           uint64_t cols, uint64_t pitch_elems, double rX, double rY)
+    {
+        unsigned colBlocks = 0;
+        int rc = haloCheck(h, cur, rows, cols, pitch_elems, &colBlocks);
+        if(rc)
+            return rc;
+        A3B_REQUIRE(next && aligned16(next) && cur != next, "bad output grid");
+        DeviceProps const* props = nullptr;
+        rc = currentDevice(&props);
+        if(rc)
+            return rc;
+        uint64_t const bands = (rows + kBand - 1) / kBand;
+        A3B_REQUIRE(bands < 65536u, "too many row bands");
+        unsigned const step = ++h->step;
+        dim3 const grid(colBlocks, static_cast<unsigned>(bands));
+        heatExchangeKernel<<<grid, kThreads, 0, static_cast<cudaStream_t>(stream)>>>(
+            cur, next, rows, cols, pitch_elems, rX, rY, mailOf(h->local, cols), mailOf(h->up, cols),
+            mailOf(h->down, cols), step, waitTimeoutNs(), props->errWord);
+        A3B_CHECK_LAUNCH("heat halo step launch");
         return A3B_OK;
     }
 

@@ -9,6 +9,8 @@ smallest data that has to move:
 * :func:`scan_carry`               scan: all-gather of the per-rank totals, carry = sum of the totals of lower ranks
 * :func:`nbody_allgather`          nBody: all-gather of the x/y/z shards into the full position arrays
 * :func:`heat_exchange_halos`      heat: one boundary row to each neighbour (send/recv), into the neighbour's ghost row
+* :class:`HeatSlab`                heat time steps on row slabs: fused stencil + halo exchange over NVLink (HaloMailbox)
+                                   or stencil + NCCL send/recv
 
 The collectives are written for tensors on the rank's device; with the gloo backend they run on CPU tensors, which
 is how the host-side logic is tested without a GPU.
@@ -182,18 +184,70 @@ class NBody:
                 nbody_allgather(full, st)
 
 
+class HaloMailbox:
+    """Halo mailbox of this rank (a3b_halo): a small device buffer that the neighbouring ranks map through CUDA IPC.
+    The fused heat step stores its boundary rows straight into the neighbours' mailboxes over NVLink and reads its
+    ghost rows from its own, with per-step flags instead of NCCL send/recv."""
+
+    def __init__(self, cols):
+        import ctypes
+        from . import capi
+        self.world, self.rank = _world()
+        L = capi.lib()
+        handle = (ctypes.c_char * L.a3b_ipc_handle_size())()
+        self.h = ctypes.c_void_p()
+        capi.call("a3b_halo_create", self.world, self.rank, cols, ctypes.byref(self.h), handle)
+        mine = bytes(handle)
+        if self.world > 1:
+            handles = [None] * self.world
+            dist.all_gather_object(handles, mine)
+        else:
+            handles = [mine]
+        blob = b"".join(handles)
+        capi.call("a3b_halo_connect", self.h, (ctypes.c_char * len(blob)).from_buffer_copy(blob))
+        if self.world > 1:
+            dist.barrier()
+
+    def close(self):
+        from . import capi
+        if self.h:
+            torch.cuda.synchronize()
+            if self.world > 1:
+                dist.barrier()  # no neighbour writes into this mailbox any more
+            capi.call("a3b_halo_destroy", self.h)
+            self.h = None
+
+
 class HeatSlab:
     """Row slab of the heat grid on one rank: `rows` interior rows (global rows row_offset+1 ... row_offset+rows) and
-    one ghost row above and below. A step updates the two boundary rows first, sends them to the neighbours (their
-    ghost rows) while the interior rows are updated, and waits for the neighbours' rows before the next step."""
+    one ghost row above and below.
 
-    def __init__(self, cur, nxt, rX, rY):
+    collective="fused" (default on several ranks): one kernel per step; its two boundary bands run first, wait for the
+    neighbours' boundary rows of the previous step in this rank's halo mailbox, and store their own boundary rows into
+    the neighbours' mailboxes over NVLink (a3b_heat_step_halo). The interior bands never wait.
+    collective="nccl": the two boundary rows are updated first, sent to the neighbours with NCCL send/recv while the
+    interior rows are updated, and the receives are waited for before the next step."""
+
+    def __init__(self, cur, nxt, rX, rY, collective="fused"):
         self.cur, self.nxt, self.rX, self.rY = cur, nxt, rX, rY
         self.rows = cur.shape[0] - 2
+        self.cols = cur.shape[1] - 2
         self.pending = []
+        self.halo = None
+        world, _ = _world()
+        if world > 1 and collective == "fused":
+            from . import algo, capi
+            self.halo = HaloMailbox(self.cols)
+            capi.call("a3b_heat_halo_publish", algo.stream_handle(), self.halo.h, algo._ptr(cur), self.rows, self.cols,
+                      cur.stride(0))
 
     def step(self):
-        from . import algo
+        from . import algo, capi
+        if self.halo is not None:
+            capi.call("a3b_heat_step_halo", algo.stream_handle(), self.halo.h, algo._ptr(self.cur),
+                      algo._ptr(self.nxt), self.rows, self.cols, self.cur.stride(0), self.rX, self.rY)
+            self.cur, self.nxt = self.nxt, self.cur
+            return
         for r in self.pending:
             r.wait()
         self.pending = []
@@ -221,6 +275,12 @@ class HeatSlab:
         for r in self.pending:
             r.wait()
         self.pending = []
+
+    def close(self):
+        self.finish()
+        if self.halo is not None:
+            self.halo.close()
+            self.halo = None
 
 
 class PeerGroup:

@@ -559,11 +559,13 @@ def run_workload(args):
         dx = 1.0 / (side + 1)
         algo.heat_init(u, dx, dx, row_offset=hb, global_rows=side)
         w = u.clone()
-        slab = adist.HeatSlab(u, w, 0.2, 0.2)
+        slab = adist.HeatSlab(u, w, 0.2, 0.2, collective=args.collective)
         fn = slab.step
         unit_bytes = 16.0 * (he - hb) * side
         total = 16.0 * side * side
-        desc = "heat 5-point stencil, 32768^2 fp64 in row slabs, one halo row exchanged with each neighbour per step"
+        desc = ("heat 5-point stencil, 32768^2 fp64 in row slabs, one halo row exchanged with each neighbour per step "
+                + ("(one kernel per step: boundary rows stored into the neighbours' mailboxes over NVLink)"
+                   if args.collective == "fused" else "(NCCL send/recv overlapped with the interior update)"))
         metric_unit = "GB/s"
 
     def step(ev):
@@ -580,7 +582,7 @@ def run_workload(args):
     _, kern = time_steps(torch, dist_on, step, args.steps, args.warmup)  # per-step events: the roofline's duration
     sampler.stop()
     if wl == "heat":
-        slab.finish()
+        slab.close()
     ms = max_over_ranks(torch, dist_on, ms)
     kern = max_over_ranks(torch, dist_on, kern)
     scale = 1e9

@@ -270,6 +270,35 @@ A3B_API int a3b_heat_init(a3b_stream_t stream, double* u, uint64_t rows, uint64_
 A3B_API int a3b_heat_exact(a3b_stream_t stream, double* u, uint64_t rows, uint64_t cols, uint64_t pitch_elems,
                            uint64_t row_offset, uint64_t global_rows, double t, double dx, double dy, int ring_only);
 
+/* Row slabs of the heat grid across the ranks of one node, halo exchange fused into the stencil step. alpaka3's
+ * heatEquation2D example runs on one device (example/heatEquation2D/src/heatEquation2D.cpp:97-214); the row
+ * decomposition with one ghost row per side is new here.
+ *
+ * Each rank owns a halo mailbox (a small cudaMalloc'd buffer: two ghost rows per side, double-buffered by step
+ * parity, and one step flag per column block) that its upper and lower neighbours map through CUDA IPC. Create it
+ * on every rank, exchange the a3b_ipc_handle_size()-byte handles (rank order), connect. */
+typedef struct a3b_halo a3b_halo;
+A3B_API size_t a3b_halo_bytes(uint64_t cols);
+A3B_API int a3b_halo_create(int world, int rank, uint64_t cols, a3b_halo** halo, void* local_handle);
+A3B_API int a3b_halo_connect(a3b_halo* halo, void const* handles);
+/* Call only when no neighbour is still writing into this mailbox (after a barrier that follows the last step). */
+A3B_API int a3b_halo_destroy(a3b_halo* halo);
+
+/* Sends this rank's first and last interior rows of u (the initial field) to the neighbours' mailboxes; call once on
+ * every rank after a3b_heat_init and before the first a3b_heat_step_halo. u: (rows + 2) x pitch_elems fp64, rows
+ * 16-byte aligned (even pitch). */
+A3B_API int a3b_heat_halo_publish(a3b_stream_t stream, a3b_halo* halo, double const* u, uint64_t rows, uint64_t cols,
+                                  uint64_t pitch_elems);
+
+/* One a3b_heat_step over the whole slab (rows 1..rows) in one launch, with the ghost rows taken from this rank's
+ * mailbox (the neighbours' boundary rows of the previous step; a rank without an upper / lower neighbour uses its
+ * own ghost row, the global Dirichlet ring) and its own boundary rows stored into the neighbours' mailboxes over
+ * NVLink. The bands holding rows 1 and `rows` run first and wait, bounded by a3b_set_wait_timeout_ns, for the
+ * neighbours' flags (a timeout raises bit 0 of the device error word); the other bands never wait. Every rank makes
+ * the same sequence of publish / step calls. */
+A3B_API int a3b_heat_step_halo(a3b_stream_t stream, a3b_halo* halo, double const* cur, double* next, uint64_t rows,
+                               uint64_t cols, uint64_t pitch_elems, double rX, double rY);
+
 #ifdef __cplusplus
 }
 #endif

@@ -95,21 +95,25 @@ def main():
     res["nbody_rel"] = max(float(np.max(np.abs(T[k + 1].cpu().numpy() - wantb[k]))) / float(np.max(np.abs(wantb[k])))
                            for k in range(3))
 
-    # heat: 256 x 256 interior split in row slabs, 9 steps, bit-exact against the oracle
-    nh = 256
-    dx = 1.0 / (nh + 1)
-    r = 0.2
-    u0 = port.heat_init(nh, dx, dx)
-    wanth = port.heat_steps(u0, nh, r, r, 9)
-    hb, he = ad.shard_range(nh, rank, world)
-    cur = torch.from_numpy(u0[hb:he + 2].copy()).to(dev)
-    nxt = cur.clone()
-    slab = ad.HeatSlab(cur, nxt, r, r)
-    for _ in range(9):
-        slab.step()
-    slab.finish()
-    torch.cuda.synchronize()
-    res["heat_ok"] = bool((slab.cur[1:he - hb + 1].cpu().numpy() == wanth[hb + 1:he + 1]).all())
+    # heat: row slabs, bit-exact against the oracle, through the fused halo exchange (mailboxes over NVLink) and
+    # through NCCL send/recv: 256 x 256 (two bands per slab) and 1000 x 1000 (eight bands per slab, a ragged last band)
+    for nh, steps in ((256, 9), (1000, 7)):
+        dx = 1.0 / (nh + 1)
+        r = 0.2
+        u0 = port.heat_init(nh, dx, dx)
+        wanth = port.heat_steps(u0, nh, r, r, steps)
+        hb, he = ad.shard_range(nh, rank, world)
+        for collective in ("fused", "nccl"):
+            cur = torch.from_numpy(u0[hb:he + 2].copy()).to(dev)
+            nxt = cur.clone()
+            slab = ad.HeatSlab(cur, nxt, r, r, collective=collective)
+            for _ in range(steps):
+                slab.step()
+            slab.close()
+            torch.cuda.synchronize()
+            ok = bool((slab.cur[1:he - hb + 1].cpu().numpy() == wanth[hb + 1:he + 1]).all())
+            key = "heat_ok" if collective == "fused" else "heat_nccl_ok"
+            res[key] = res.get(key, True) and ok
 
     allres = [None] * world
     torch.distributed.all_gather_object(allres, res)

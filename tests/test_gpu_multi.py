@@ -27,7 +27,7 @@ def test_sharded_algorithms_two_ranks(cuda):
     for r in out["ranks"]:
         assert r["sumsq_rel"] <= 1e-5
         assert r["dot_rel"] <= 1e-12
-        assert r["min_ok"] and r["scan_i32_ok"] and r["scan_u64_ok"] and r["heat_ok"]
+        assert r["min_ok"] and r["scan_i32_ok"] and r["scan_u64_ok"] and r["heat_ok"] and r["heat_nccl_ok"]
         assert r["nbody_rel"] <= 1e-4
         assert r["sumsq_fused_rel"] <= 1e-5 and r["fused_matches_nccl"] and r["fused_repeat_ok"] and r["fused_max_ok"]
         assert r["peer_scan_ok"]
