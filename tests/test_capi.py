@@ -54,3 +54,17 @@ def test_invalid_arguments_rejected_without_gpu():
     rc = L.a3b_babelstream(None, capi.TRIAD, capi.I32, None, None, None, 10, 0.4, None)
     assert rc == capi.ERR_INVALID
     assert "null" in capi.last_error()
+
+
+def test_halo_mailbox_layout_and_argument_checks_without_gpu():
+    """heat halo mailbox: 16 KB of step flags (2 sides x 2 parities x 1024 column blocks) + 4 ghost rows of cols + 2
+    doubles padded to 256 bytes; steps and publications on a missing or unconnected mailbox are rejected up front."""
+    from alpaka3_b200 import capi
+    L = capi.lib()
+    for cols in (1, 1000, 32768):
+        row = -(-(cols + 2) // 32) * 32
+        assert L.a3b_halo_bytes(cols) == 2 * 2 * 1024 * 4 + 4 * row * 8
+    assert L.a3b_heat_step_halo(None, None, None, None, 10, 10, 12, 0.2, 0.2) == capi.ERR_INVALID
+    assert "halo" in capi.last_error()
+    assert L.a3b_heat_halo_publish(None, None, None, 10, 10, 12) == capi.ERR_INVALID
+    assert L.a3b_halo_destroy(None) == capi.OK
