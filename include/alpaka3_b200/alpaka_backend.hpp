@@ -5,6 +5,8 @@
  *   alpaka::onHost::reduce            (include/alpaka/onHost/algo/reduce.hpp:28-79)
  *   alpaka::onHost::exclusiveScan / inclusiveScan / *InPlace   (include/alpaka/onHost/algo/scan.hpp:45-218)
  *   alpaka::onHost::transform         (include/alpaka/onHost/algo/transform.hpp:50-88; nvcc translation units only)
+ *   alpaka::onHost::iota              (include/alpaka/onHost/algo/iota.hpp:29-85)
+ *   alpaka::onHost::fill              (include/alpaka/onHost/Queue.hpp:346)
  * for queues of CUDA devices (Queue<Device<api::Cuda, K>, Q>). Partial ordering picks them over alpaka3's generic
  * templates because their queue parameter is more specialised. At run time a call goes to the C ABI when
  *   - the element type is int32/uint32/int64/uint64/float/double,
@@ -15,6 +17,8 @@
  * transform with any functor that takes alpaka::Simd packs (or a ScalarFunc taking scalars) and no accelerator, on
  * device buffers of equal extents laid out densely or as pitched rows, runs the B200 element-wise engine of
  * elementwise.cuh, compiled here by nvcc with the caller's functor;
+ * fill of a dense buffer of those element types, and iota into one dense integer buffer of the iota's own type
+ * (alpaka3's floating-point iota rounds per SIMD pack, so it stays on alpaka3's kernel), go to a3b_fill / a3b_iota;
  * every other call is forwarded unchanged to alpaka3's own implementation (onHost::internal::transformReduce /
  * internal::scan), so the caller's results never depend on the routing. Backend errors throw std::runtime_error, as
  * alpaka3's ALPAKA_UNIFORM_CUDA_HIP_RT_CHECK does (include/alpaka/core/UniformCudaHip.hpp:42). Blocking queues wait
@@ -436,6 +440,48 @@ namespace alpaka3_b200
         }
 #endif
 
+        // Route fill to the C ABI; false when the call is not covered.
+        template<typename Q, typename T>
+        bool tryFill(Q const& queue, auto& dest, T const& value)
+        {
+            constexpr int dt = dtypeOf<std::remove_const_t<T>>();
+            if constexpr(dt < 0 || !alpaka::concepts::IMdSpan<std::decay_t<decltype(dest)>>)
+                return false;
+            else
+            {
+                Layout l;
+                if(!layoutOf<std::remove_const_t<T>>(dest, l) || !l.dense())
+                    return false;
+                check(a3b_fill(streamOf(queue), dt, const_cast<void*>(l.ptr), l.rows * l.rowLen, &value),
+                      "alpaka3_b200 fill");
+                finish(queue);
+                ++routingStats().routed;
+                return true;
+            }
+        }
+
+        // Route iota to the C ABI: one dense output of an integer type equal to the iota's type (the values are then
+        // exact whatever the order of the additions); false when the call is not covered.
+        template<typename T, typename Q>
+        bool tryIota(Q const& queue, T const& init, auto& out, auto const&... others)
+        {
+            using V = std::remove_const_t<alpaka::trait::GetValueType_t<std::decay_t<decltype(out)>>>;
+            constexpr int dt = dtypeOf<V>();
+            if constexpr(sizeof...(others) != 0 || dt < 0 || !std::is_integral_v<V> || !std::is_same_v<V, T>)
+                return false;
+            else
+            {
+                Layout l;
+                if(!layoutOf<V>(out, l) || !l.dense())
+                    return false;
+                check(a3b_iota(streamOf(queue), dt, const_cast<void*>(l.ptr), l.rows * l.rowLen, &init),
+                      "alpaka3_b200 iota");
+                finish(queue);
+                ++routingStats().routed;
+                return true;
+            }
+        }
+
         template<typename Q>
         auto resolveExec(Q const& queue, auto exec)
         {
@@ -601,6 +647,65 @@ namespace alpaka::onHost
     ALPAKA3_B200_SCAN_OVERLOADS(exclusiveScan, false, EXCLUSIVE_SCAN)
     ALPAKA3_B200_SCAN_OVERLOADS(inclusiveScan, true, INCLUSIVE_SCAN)
 #undef ALPAKA3_B200_SCAN_OVERLOADS
+    // ----------------------------------------------------------------------------------------------------- iota
+    template<typename T_DataType, alpaka::concepts::DeviceKind T_DeviceKind, alpaka::concepts::QueueKind T_QueueKind>
+    requires(std::is_fundamental_v<T_DataType>)
+    inline void iota(
+        Queue<Device<api::Cuda, T_DeviceKind>, T_QueueKind> const& queue,
+        alpaka::concepts::Executor auto const exec,
+        T_DataType const& initValue,
+        alpaka::concepts::IMdSpan auto&& out0,
+        alpaka::concepts::IMdSpan auto&&... outOther)
+        requires(
+            std::is_convertible_v<T_DataType, alpaka::trait::GetValueType_t<ALPAKA_TYPEOF(out0)>>
+            && std::conjunction_v<
+                std::is_convertible<T_DataType, typename alpaka::trait::GetValueType_t<ALPAKA_TYPEOF(outOther)>>...>)
+    {
+        if(alpaka3_b200::detail::tryIota(queue, initValue, out0, outOther...))
+            return;
+        ++alpaka3_b200::routingStats().forwarded;
+        internal::iota<T_DataType>(
+            queue,
+            alpaka3_b200::detail::resolveExec(queue, exec),
+            onHost::getExtents(out0),
+            initValue,
+            ALPAKA_FORWARD(out0),
+            ALPAKA_FORWARD(outOther)...);
+    }
+
+    template<typename T_DataType, alpaka::concepts::DeviceKind T_DeviceKind, alpaka::concepts::QueueKind T_QueueKind>
+    requires(std::is_fundamental_v<T_DataType>)
+    inline void iota(
+        Queue<Device<api::Cuda, T_DeviceKind>, T_QueueKind> const& queue,
+        T_DataType const& initValue,
+        alpaka::concepts::IMdSpan auto&& out0,
+        alpaka::concepts::IMdSpan auto&&... outOther)
+        requires(
+            std::is_convertible_v<T_DataType, alpaka::trait::GetValueType_t<ALPAKA_TYPEOF(out0)>>
+            && std::conjunction_v<
+                std::is_convertible<T_DataType, typename alpaka::trait::GetValueType_t<ALPAKA_TYPEOF(outOther)>>...>)
+    {
+        iota<T_DataType>(
+            queue,
+            defaultExecutor(queue.getDevice()),
+            initValue,
+            ALPAKA_FORWARD(out0),
+            ALPAKA_FORWARD(outOther)...);
+    }
+
+    // ----------------------------------------------------------------------------------------------------- fill
+    template<typename T_Value, alpaka::concepts::DeviceKind T_DeviceKind, alpaka::concepts::QueueKind T_QueueKind>
+    inline void fill(Queue<Device<api::Cuda, T_DeviceKind>, T_QueueKind> const& queue, auto&& dest, T_Value elementValue)
+        requires(
+            std::same_as<alpaka::trait::GetValueType_t<ALPAKA_TYPEOF(dest)>, T_Value>
+            && std::same_as<ALPAKA_TYPEOF(alpaka::internal::getApi(queue)), ALPAKA_TYPEOF(alpaka::internal::getApi(dest))>)
+    {
+        if(alpaka3_b200::detail::tryFill(queue, dest, elementValue))
+            return;
+        ++alpaka3_b200::routingStats().forwarded;
+        fill(queue, ALPAKA_FORWARD(dest), elementValue, internal::getExtents(dest));
+    }
+
     // ------------------------------------------------------------------------------------------------ transform
     template<alpaka::concepts::DeviceKind T_DeviceKind, alpaka::concepts::QueueKind T_QueueKind>
     inline void transform(

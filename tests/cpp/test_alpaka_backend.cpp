@@ -6,7 +6,8 @@
  * plus BabelStream's dot (benchmark/babelstream/src/babelStreamMainTest.cpp:135-141, 337-345), and
  * test/unit/algorithm/transform.cpp:147-180 (int inputs over the same N-D extents with std::minus, std::plus, a
  * StencilFunc, ScalarFunc with and without an accelerator argument, and an up-casting functor), plus an in-place
- * transform of a large 1-D float array with a ragged end.
+ * transform of a large 1-D float array with a ragged end, test/unit/algorithm/iota.cpp:13-118 (size_t iota over the
+ * same extents, into one buffer and into two) and element-wise fill.
  * Prints one line "PASS routed=<n> forwarded=<m>" and exits 0, or lists the failures and exits 1. */
 #include <alpaka3_b200/alpaka_backend.hpp>
 
@@ -259,6 +260,52 @@ namespace
         }
     }
 
+    //! iota<size_t> with init 42 into one buffer, then init 43 into two (test/unit/algorithm/iota.cpp:13-85); element
+    //! by element in the extents' row-major order. One dense output goes to the C ABI, two outputs to alpaka3.
+    void iotaOne(auto& dev, auto& queue, auto exec, auto extents)
+    {
+        using T = std::size_t;
+        auto b0 = onHost::alloc<T>(dev, extents);
+        auto b1 = onHost::allocLike(dev, b0);
+        auto h0 = onHost::allocHostLike(b0);
+        auto h1 = onHost::allocHostLike(b1);
+        for(int outputs = 1; outputs <= 2; ++outputs)
+        {
+            T const init = outputs == 1 ? T{42} : T{43};
+            onHost::memset(queue, b0, 0u);
+            onHost::memset(queue, b1, 0u);
+            if(outputs == 1)
+                onHost::iota<T>(queue, exec, init, b0);
+            else
+                onHost::iota<T>(queue, exec, init, b0, b1);
+            onHost::memcpy(queue, h0, b0);
+            onHost::memcpy(queue, h1, b1);
+            onHost::wait(queue);
+            T want = init;
+            int bad = 0;
+            auto it1 = h1.begin();
+            for(auto const& v : h0)
+            {
+                T const w1 = *it1;
+                ++it1;
+                if((v != want || (outputs == 2 && w1 != want)) && bad++ < 3)
+                    expect(false, outputs == 1 ? "iota" : "iota two outputs", static_cast<long long>(v),
+                           static_cast<long long>(want));
+                ++want;
+            }
+        }
+        // fill: element-wise value into the same buffer
+        onHost::fill(queue, b0, T{7});
+        onHost::memcpy(queue, h0, b0);
+        onHost::wait(queue);
+        for(auto const& v : h0)
+            if(v != T{7})
+            {
+                expect(false, "fill", static_cast<long long>(v), 7);
+                break;
+            }
+    }
+
     template<typename T>
     T hostReduce(int op, std::size_t n, T init)
     {
@@ -356,6 +403,16 @@ int main()
     transformTests(dev, queue, exec, Vec{7, 3});
     transformTests(dev, queue, exec, Vec{3});
     transformLarge(dev, queue, exec);
+    // extents of test/unit/algorithm/iota.cpp:112-113
+    auto const routedBeforeIota = alpaka3_b200::routingStats().routed.load();
+    iotaOne(dev, queue, exec, Vec{5, 7, 3, 11});
+    iotaOne(dev, queue, exec, Vec{93, 7, 123});
+    iotaOne(dev, queue, exec, Vec{5, 7, 4111});
+    iotaOne(dev, queue, exec, Vec{5, 7, 3});
+    iotaOne(dev, queue, exec, Vec{7, 3});
+    iotaOne(dev, queue, exec, Vec{3});
+    std::printf("iota/fill routed=%llu\n",
+                static_cast<unsigned long long>(alpaka3_b200::routingStats().routed.load() - routedBeforeIota));
     auto& st = alpaka3_b200::routingStats();
     if(failures == 0)
         std::printf("PASS routed=%llu forwarded=%llu\n", static_cast<unsigned long long>(st.routed.load()),

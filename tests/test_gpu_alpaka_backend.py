@@ -26,3 +26,7 @@ def test_alpaka_api_through_binding(cuda):
     # functors that take an accelerator)
     assert routed >= 4 * 8 + 6 * 3 + 1 + 6 * 4 + 1, p.stdout
     assert forwarded >= 6 + 1 + 6 * 3, p.stdout
+    # iota into one dense buffer and fill go to the C ABI (at least the 1-D extent is dense); iota into two buffers
+    # stays on alpaka3's kernel
+    m = re.search(r"iota/fill routed=(\d+)", p.stdout)
+    assert m and int(m.group(1)) >= 2, p.stdout
