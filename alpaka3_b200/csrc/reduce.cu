@@ -500,6 +500,12 @@ namespace a3b
         // the world's values in its own buffer and combines them in rank order: every rank computes the same bits.
         // With lowerRanksOnly the combination covers ranks 0 .. rank-1 (the carry of a scan split across ranks); the
         // wait still covers every rank, so one call's slots are never overwritten by the next call too early.
+        //
+        // Consecutive calls on a stream overlap (programmatic dependent launch): every block lets the next call's
+        // kernel launch as soon as it has started, and waits for the previous call's kernel to complete only after
+        // its own pass over the input, before it touches the scratch, the slots or `out`. The next call's HBM pass
+        // thus runs while this call waits for the other ranks, and at most two calls are in flight (a call's blocks
+        // cannot retire before the previous call completes), which the two slot parities cover.
         template<typename T, int W, int ROp, int XOp, bool LOOP>
         __global__ void __launch_bounds__(kBlock) reduceAllRanksKernel(
             T const* __restrict__ in0,
@@ -517,8 +523,11 @@ namespace a3b
             using A = typename AccOf<T, ROp>::type;
             __shared__ A smem[kWarps];
             __shared__ bool flag;
+            if(threadIdx.x == 0)
+                asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
             A const neutralA = widen<A>(neutral);
             A const v = blockPartial<T, W, ROp, XOp, false, LOOP>(in0, in1, n, n, 0, neutral, ppt, smem);
+            asm volatile("griddepcontrol.wait;" ::: "memory"); // the previous call on this stream has completed
             A r;
             if(!combineGrid<A, ROp>(v, neutralA, work, smem, &flag, &r))
                 return;
@@ -598,13 +607,23 @@ namespace a3b
             if(rc)
                 return rc;
             auto const w = workAt<A>(scr, kMaxGroups);
+            cudaLaunchAttribute attr[1];
+            attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+            attr[0].val.programmaticStreamSerializationAllowed = 1;
+            cudaLaunchConfig_t cfg = {};
+            cfg.gridDim = dim3(static_cast<unsigned>(grid));
+            cfg.blockDim = dim3(kBlock);
+            cfg.dynamicSmemBytes = 0;
+            cfg.stream = s;
+            cfg.attrs = attr;
+            cfg.numAttrs = 1;
+            uint64_t const to = waitTimeoutNs();
             if(loop)
-                reduceAllRanksKernel<T, W, ROp, XOp, true><<<static_cast<unsigned>(grid), kBlock, 0, s>>>(
-                    in0, in1, n, neutral, ppt, out, w, peers, lower, props->errWord, waitTimeoutNs());
+                A3B_CUDA(cudaLaunchKernelEx(&cfg, reduceAllRanksKernel<T, W, ROp, XOp, true>, in0, in1, n, neutral, ppt,
+                                            out, w, peers, lower, props->errWord, to));
             else
-                reduceAllRanksKernel<T, W, ROp, XOp, false><<<static_cast<unsigned>(grid), kBlock, 0, s>>>(
-                    in0, in1, n, neutral, ppt, out, w, peers, lower, props->errWord, waitTimeoutNs());
-            A3B_CHECK_LAUNCH("transform_reduce_allranks launch");
+                A3B_CUDA(cudaLaunchKernelEx(&cfg, reduceAllRanksKernel<T, W, ROp, XOp, false>, in0, in1, n, neutral,
+                                            ppt, out, w, peers, lower, props->errWord, to));
             return A3B_OK;
         }
 
