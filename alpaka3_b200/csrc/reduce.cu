@@ -23,6 +23,9 @@
 #include <mutex>
 #include <type_traits>
 
+#include <map>
+#include <utility>
+
 #include "common.cuh"
 
 namespace a3b
@@ -503,7 +506,8 @@ namespace a3b
         //
         // Consecutive calls on a stream overlap (programmatic dependent launch): every block lets the next call's
         // kernel launch as soon as it has started, and waits for the previous call's kernel to complete only after
-        // its own pass over the input, before it touches the scratch, the slots or `out`. The next call's HBM pass
+        // its own pass over the input, before it touches the scratch, the slots or `out` (a call whose input overlaps
+        // the previous call's `out` is launched without the early start). The next call's HBM pass
         // thus runs while this call waits for the other ranks, and at most two calls are in flight (a call's blocks
         // cannot retire before the previous call completes), which the two slot parities cover.
         template<typename T, int W, int ROp, int XOp, bool LOOP>
@@ -585,6 +589,30 @@ namespace a3b
             writeResult<T, A>(out, total, false);
         }
 
+        // The output range of the last fused call launched on each (device, stream). A call whose input overlaps it
+        // must see that output completely, so it is launched without the early start.
+        struct LastOut
+        {
+            uintptr_t lo = 0, hi = 0;
+        };
+        std::mutex gLastOutMutex;
+        std::map<std::pair<int, cudaStream_t>, LastOut> gLastOut;
+
+        bool overlapsLastOut(int dev, cudaStream_t s, void const* in0, void const* in1, uint64_t inBytes, void* out)
+        {
+            std::lock_guard<std::mutex> lock(gLastOutMutex);
+            LastOut& l = gLastOut[std::make_pair(dev, s)];
+            auto hit = [&](void const* p)
+            {
+                auto const a = reinterpret_cast<uintptr_t>(p);
+                return p && a < l.hi && l.lo < a + inBytes;
+            };
+            bool const overlap = hit(in0) || hit(in1);
+            l.lo = reinterpret_cast<uintptr_t>(out);
+            l.hi = l.lo + 8u;
+            return overlap;
+        }
+
         template<typename T, int W, int ROp, int XOp>
         int launchAllRanks(cudaStream_t s, a3b_peer_group* g, T const* in0, T const* in1, uint64_t n, T neutral, void* out,
                            bool lower)
@@ -616,7 +644,7 @@ namespace a3b
             cfg.dynamicSmemBytes = 0;
             cfg.stream = s;
             cfg.attrs = attr;
-            cfg.numAttrs = 1;
+            cfg.numAttrs = overlapsLastOut(props->ordinal, s, in0, in1, n * sizeof(T), out) ? 0 : 1;
             uint64_t const to = waitTimeoutNs();
             if(loop)
                 A3B_CUDA(cudaLaunchKernelEx(&cfg, reduceAllRanksKernel<T, W, ROp, XOp, true>, in0, in1, n, neutral, ppt,

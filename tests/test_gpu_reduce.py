@@ -133,3 +133,33 @@ def test_partial_is_unrounded(cuda, port):
     assert p.dtype == torch.float64
     exact = port.sumsq(x.cpu().numpy())
     assert abs(p.item() - exact) / exact < 1e-9
+
+
+def test_fused_reduce_one_rank_back_to_back_and_chained(cuda, port):
+    """The fused reduce + all-reduce on a one-rank peer group: consecutive calls overlap on the stream (the next call
+    reads its input while the previous one finishes), so repeated calls must give the same bits, and a call whose
+    input starts with the previous call's output must see that output (it is launched without the early start)."""
+    from alpaka3_b200 import algo, dist as adist
+    from oracle.oracle import SEED
+    n = (1 << 24) + 7
+    x = torch.empty(n, dtype=torch.float32, device=cuda)
+    algo.random_f32(x, SEED, -1.0, 1.0)
+    want = port.sumsq(port.gen_f32(n, -1.0, 1.0))
+    g = adist.PeerGroup()
+    try:
+        outs = [torch.empty(1, dtype=torch.float32, device=cuda) for _ in range(8)]
+        for o in outs:
+            g.transform_reduce(0.0, "plus", "square", x, out=o)
+        vals = [float(o.item()) for o in outs]
+        assert all(v == vals[0] for v in vals)
+        assert abs(vals[0] - want) / want <= 1e-5
+        # chain: buf[0] receives a sum, the next call reduces buf (identity), whose other elements are 0
+        buf = torch.zeros(64, dtype=torch.float32, device=cuda)
+        total = torch.empty(1, dtype=torch.float32, device=cuda)
+        for _ in range(4):
+            g.transform_reduce(0.0, "plus", "square", x, out=buf[0:1])
+            g.transform_reduce(0.0, "plus", "identity", buf, out=total)
+            torch.cuda.synchronize()
+            assert float(total.item()) == float(buf[0].item()) == vals[0]
+    finally:
+        g.close()
