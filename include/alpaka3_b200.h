@@ -201,7 +201,10 @@ A3B_API int a3b_peer_group_destroy(a3b_peer_group* group);
  * per rank reduces the local shard, its last block stores the unrounded partial into every rank's slot (peer stores
  * over NVLink), waits (bounded) for all ranks' partials and combines them in rank order, so every rank writes the
  * same bits to its `out`. All ranks must make the same sequence of calls. A wait that runs out sets bit 0 of the
- * device error word (a3b_get_device_error). */
+ * device error word (a3b_get_device_error). Consecutive calls on one stream overlap (programmatic dependent launch):
+ * a call reads its input while the previous call still waits for the other ranks, and touches its scratch, the slots
+ * and `out` only after that call has completed. A call whose input overlaps the previous call's `out` is launched
+ * fully ordered instead; input written by any other kernel or copy is always complete before the call reads it. */
 A3B_API int a3b_transform_reduce_allranks(a3b_stream_t stream, a3b_peer_group* group, int dtype, int reduce_op,
                                           int transform_op, void const* in0, void const* in1, uint64_t n,
                                           void const* neutral, void* out);
