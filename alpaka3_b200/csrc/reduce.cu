@@ -467,11 +467,6 @@ namespace a3b
             asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
         }
 
-        __device__ __forceinline__ void stReleaseSys(unsigned long long* p, unsigned long long v)
-        {
-            asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
-        }
-
         __device__ __forceinline__ unsigned long long ldAcquireSys(unsigned long long const* p)
         {
             unsigned long long v;
