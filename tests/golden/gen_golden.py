@@ -2,7 +2,7 @@
 reference headers by oracle/build_ref.sh) on the inputs the reference's unit tests and examples use.
 
 Run here (where the reference tree exists):  python tests/golden/gen_golden.py
-The fixtures are small (hashes, scalars, a few KB of arrays) and are committed; the GPU box never needs the reference.
+The fixtures are small (hashes, scalars, a few KB of arrays) and are committed; the tests never read the reference.
 
   scan_iota.json      test/unit/algorithm/scan.cpp:158-197: int iota 0..n-1, n in {12, 1024, 654321, 20971520},
                       exclusive and inclusive (int wraps at 20 Mi): sha256 of the int32 output + head/tail values

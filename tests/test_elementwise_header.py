@@ -1,6 +1,6 @@
 """CPU: the header-only element-wise engine (include/alpaka3_b200/elementwise.cuh) compiles on its own, without
-alpaka3, for sm_100a, with the standalone call INTEGRATION.md shows (nvcc cross-compiles here; the engine runs on the
-GPU through the alpaka3 binding test)."""
+alpaka3, for sm_100a, used directly as a library user would (nvcc cross-compiles without a GPU; the engine itself runs
+on the GPU in the alpaka3 binding test)."""
 import os
 import shutil
 import subprocess
