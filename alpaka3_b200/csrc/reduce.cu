@@ -437,7 +437,10 @@ namespace a3b
             return true;
         }
 
-        template<typename T, int W, int ROp, int XOp, bool PITCHED, bool LOOP>
+        // PDL: the kernel overlaps the previous kernel of its stream (launched with programmatic stream
+        // serialisation): it lets the next call launch once it has started and waits for the previous call only after
+        // its pass over the input, before touching the scratch or `out`.
+        template<typename T, int W, int ROp, int XOp, bool PITCHED, bool LOOP, bool PDL>
         __global__ void __launch_bounds__(kBlock) reduceKernel(
             T const* __restrict__ in0,
             T const* __restrict__ in1,
@@ -453,12 +456,43 @@ namespace a3b
             using A = typename AccOf<T, ROp>::type;
             __shared__ A smem[kWarps];
             __shared__ bool flag;
+            if constexpr(PDL)
+            {
+                if(threadIdx.x == 0)
+                    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+            }
             A const v = blockPartial<T, W, ROp, XOp, PITCHED, LOOP>(in0, in1, n, rowLen, rowPitch, neutral, ppt, smem);
+            if constexpr(PDL)
+                asm volatile("griddepcontrol.wait;" ::: "memory"); // the previous call on this stream has completed
             A total;
             if(!combineGrid<A, ROp>(v, widen<A>(neutral), work, smem, &flag, &total))
                 return;
             if(threadIdx.x == 0)
                 writeResult<T, A>(out, total, rawPartial);
+        }
+
+        // The output range of the last reduction launched with the early start on each (device, stream). A call whose
+        // input overlaps it must see that output completely, so it is launched without the early start.
+        struct LastOut
+        {
+            uintptr_t lo = 0, hi = 0;
+        };
+        std::mutex gLastOutMutex;
+        std::map<std::pair<int, cudaStream_t>, LastOut> gLastOut;
+
+        bool overlapsLastOut(int dev, cudaStream_t s, void const* in0, void const* in1, uint64_t inBytes, void* out)
+        {
+            std::lock_guard<std::mutex> lock(gLastOutMutex);
+            LastOut& l = gLastOut[std::make_pair(dev, s)];
+            auto hit = [&](void const* p)
+            {
+                auto const a = reinterpret_cast<uintptr_t>(p);
+                return p && a < l.hi && l.lo < a + inBytes;
+            };
+            bool const overlap = hit(in0) || hit(in1);
+            l.lo = reinterpret_cast<uintptr_t>(out);
+            l.hi = l.lo + 8u;
+            return overlap;
         }
 
         // ---------------------------------------------------------------- fused with the all-reduce over peers
@@ -584,30 +618,6 @@ namespace a3b
             writeResult<T, A>(out, total, false);
         }
 
-        // The output range of the last fused call launched on each (device, stream). A call whose input overlaps it
-        // must see that output completely, so it is launched without the early start.
-        struct LastOut
-        {
-            uintptr_t lo = 0, hi = 0;
-        };
-        std::mutex gLastOutMutex;
-        std::map<std::pair<int, cudaStream_t>, LastOut> gLastOut;
-
-        bool overlapsLastOut(int dev, cudaStream_t s, void const* in0, void const* in1, uint64_t inBytes, void* out)
-        {
-            std::lock_guard<std::mutex> lock(gLastOutMutex);
-            LastOut& l = gLastOut[std::make_pair(dev, s)];
-            auto hit = [&](void const* p)
-            {
-                auto const a = reinterpret_cast<uintptr_t>(p);
-                return p && a < l.hi && l.lo < a + inBytes;
-            };
-            bool const overlap = hit(in0) || hit(in1);
-            l.lo = reinterpret_cast<uintptr_t>(out);
-            l.hi = l.lo + 8u;
-            return overlap;
-        }
-
         template<typename T, int W, int ROp, int XOp>
         int launchAllRanks(cudaStream_t s, a3b_peer_group* g, T const* in0, T const* in1, uint64_t n, T neutral, void* out,
                            bool lower)
@@ -707,6 +717,7 @@ namespace a3b
             }
         }
 
+
         template<typename T, int W, int ROp, int XOp, bool PITCHED>
         int launchReduce(
             cudaStream_t s,
@@ -733,13 +744,23 @@ namespace a3b
             if(rc)
                 return rc;
             auto const w = workAt<A>(scr, kMaxGroups);
+            uint64_t const rows = PITCHED ? (n + rowLen - 1) / rowLen : 1u;
+            uint64_t const inBytes = PITCHED ? rows * rowPitch : n * sizeof(T);
+            cudaLaunchAttribute attr[1];
+            attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+            attr[0].val.programmaticStreamSerializationAllowed = 1;
+            cudaLaunchConfig_t cfg = {};
+            cfg.gridDim = dim3(static_cast<unsigned>(grid));
+            cfg.blockDim = dim3(kBlock);
+            cfg.stream = s;
+            cfg.attrs = attr;
+            cfg.numAttrs = overlapsLastOut(props->ordinal, s, in0, in1, inBytes, out) ? 0 : 1;
             if(loop)
-                reduceKernel<T, W, ROp, XOp, PITCHED, true><<<static_cast<unsigned>(grid), kBlock, 0, s>>>(
-                    in0, in1, n, rowLen, rowPitch, neutral, ppt, out, raw, w);
+                A3B_CUDA(cudaLaunchKernelEx(&cfg, reduceKernel<T, W, ROp, XOp, PITCHED, true, true>, in0, in1, n, rowLen,
+                                            rowPitch, neutral, ppt, out, raw, w));
             else
-                reduceKernel<T, W, ROp, XOp, PITCHED, false><<<static_cast<unsigned>(grid), kBlock, 0, s>>>(
-                    in0, in1, n, rowLen, rowPitch, neutral, ppt, out, raw, w);
-            A3B_CHECK_LAUNCH("transform_reduce launch");
+                A3B_CUDA(cudaLaunchKernelEx(&cfg, reduceKernel<T, W, ROp, XOp, PITCHED, false, true>, in0, in1, n, rowLen,
+                                            rowPitch, neutral, ppt, out, raw, w));
             return A3B_OK;
         }
 
@@ -944,7 +965,7 @@ namespace a3b
                 return rc;
             // the array keeps the previous call's contents: the tickets must start at zero
             A3B_CUDA(cudaMemsetAsync(scr, 0, 64u + roundUp64(sizeof(unsigned) * kNoAllocGroups), s));
-            reduceKernel<T, W, ROp, XOp, false, true><<<static_cast<unsigned>(grid), kBlock, 0, s>>>(
+            reduceKernel<T, W, ROp, XOp, false, true, false><<<static_cast<unsigned>(grid), kBlock, 0, s>>>(
                 in0, in1, n, n, 0, neutral, ppt, out, false, workAt<A>(scr, kNoAllocGroups));
             A3B_CHECK_LAUNCH("transform_reduce_noalloc launch");
             return A3B_OK;

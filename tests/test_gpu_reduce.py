@@ -163,3 +163,32 @@ def test_fused_reduce_one_rank_back_to_back_and_chained(cuda, port):
             assert float(total.item()) == float(buf[0].item()) == vals[0]
     finally:
         g.close()
+
+
+def test_plain_reduce_back_to_back_and_chained(cuda, port):
+    """Consecutive transformReduce calls on a stream overlap (the next call reads its input while the previous one
+    combines its partials): repeated calls give the same bits, and a call whose input starts with the previous call's
+    output sees that output, for the dense and the pitched kernel."""
+    from alpaka3_b200 import algo
+    from oracle.oracle import SEED
+    n = (1 << 24) + 7
+    x = torch.empty(n, dtype=torch.float32, device=cuda)
+    algo.random_f32(x, SEED, -1.0, 1.0)
+    want = port.sumsq(port.gen_f32(n, -1.0, 1.0))
+    outs = [torch.empty(1, dtype=torch.float32, device=cuda) for _ in range(8)]
+    for o in outs:
+        algo.transform_reduce(0.0, o, "plus", "square", x)
+    vals = [float(o.item()) for o in outs]
+    assert all(v == vals[0] for v in vals) and abs(vals[0] - want) / want <= 1e-5
+    buf = torch.zeros(64, dtype=torch.float32, device=cuda)
+    grid = torch.zeros((4, 40), dtype=torch.float32, device=cuda)  # pitched rows of 32 columns
+    total = torch.empty(1, dtype=torch.float32, device=cuda)
+    for _ in range(4):
+        algo.transform_reduce(0.0, buf[0:1], "plus", "square", x)
+        algo.transform_reduce(0.0, total, "plus", "identity", buf)
+        torch.cuda.synchronize()
+        assert float(total.item()) == float(buf[0].item()) == vals[0]
+        algo.transform_reduce(0.0, grid[1, 3:4], "plus", "square", x)
+        algo.reduce(0.0, total, "plus", grid[:, :32])
+        torch.cuda.synchronize()
+        assert float(total.item()) == vals[0]
