@@ -25,6 +25,7 @@
 
 #include <map>
 #include <utility>
+#include <vector>
 
 #include "common.cuh"
 
@@ -438,8 +439,10 @@ namespace a3b
         }
 
         // PDL: the kernel overlaps the previous kernel of its stream (launched with programmatic stream
-        // serialisation): it lets the next call launch once it has started and waits for the previous call only after
-        // its pass over the input, before touching the scratch or `out`.
+        // serialisation): it lets the next call launch once it has started, and waits for the previous call only
+        // after its pass over the input, before touching the scratch or `out`. Several calls can be in flight; each
+        // one's scratch and `out` accesses still follow the previous call's completion (host-side guard: see
+        // earlyStartAllowed).
         template<typename T, int W, int ROp, int XOp, bool PITCHED, bool LOOP, bool PDL>
         __global__ void __launch_bounds__(kBlock) reduceKernel(
             T const* __restrict__ in0,
@@ -471,28 +474,40 @@ namespace a3b
                 writeResult<T, A>(out, total, rawPartial);
         }
 
-        // The output range of the last reduction launched with the early start on each (device, stream). A call whose
-        // input overlaps it must see that output completely, so it is launched without the early start.
-        struct LastOut
-        {
-            uintptr_t lo = 0, hi = 0;
-        };
-        std::mutex gLastOutMutex;
-        std::map<std::pair<int, cudaStream_t>, LastOut> gLastOut;
+        // Outputs of the reductions launched with the early start on each (device, stream) since the last one launched
+        // fully ordered. Such a call may still be running while a later call of the stream reads its input (that read
+        // comes before the later call's griddepcontrol.wait). A call whose input overlaps one of these outputs, or a
+        // history grown past kMaxEarly entries, is launched fully ordered, which also clears the history: a plain
+        // launch starts only after all earlier work of the stream has completed.
+        constexpr size_t kMaxEarly = 64;
+        std::mutex gEarlyMutex;
+        std::map<std::pair<int, cudaStream_t>, std::vector<std::pair<uintptr_t, uintptr_t>>> gEarlyOutputs;
 
-        bool overlapsLastOut(int dev, cudaStream_t s, void const* in0, void const* in1, uint64_t inBytes, void* out)
+        // true: launch with the early start; in both cases `out` (8 bytes) joins the stream's history
+        bool earlyStartAllowed(int dev, cudaStream_t s, void const* in0, void const* in1, uint64_t inBytes, void* out)
         {
-            std::lock_guard<std::mutex> lock(gLastOutMutex);
-            LastOut& l = gLastOut[std::make_pair(dev, s)];
+            std::lock_guard<std::mutex> lock(gEarlyMutex);
+            auto& h = gEarlyOutputs[std::make_pair(dev, s)];
             auto hit = [&](void const* p)
             {
+                if(!p)
+                    return false;
                 auto const a = reinterpret_cast<uintptr_t>(p);
-                return p && a < l.hi && l.lo < a + inBytes;
+                for(auto const& r : h)
+                    if(a < r.second && r.first < a + inBytes)
+                        return true;
+                return false;
             };
-            bool const overlap = hit(in0) || hit(in1);
-            l.lo = reinterpret_cast<uintptr_t>(out);
-            l.hi = l.lo + 8u;
-            return overlap;
+            bool const early = !(hit(in0) || hit(in1)) && h.size() < kMaxEarly;
+            if(!early)
+                h.clear();
+            auto const o = reinterpret_cast<uintptr_t>(out);
+            bool known = false;
+            for(auto const& r : h)
+                known = known || (r.first == o && r.second == o + 8u);
+            if(!known)
+                h.emplace_back(o, o + 8u);
+            return early;
         }
 
         // ---------------------------------------------------------------- fused with the all-reduce over peers
@@ -534,11 +549,11 @@ namespace a3b
         // wait still covers every rank, so one call's slots are never overwritten by the next call too early.
         //
         // Consecutive calls on a stream overlap (programmatic dependent launch): every block lets the next call's
-        // kernel launch as soon as it has started, and waits for the previous call's kernel to complete only after
-        // its own pass over the input, before it touches the scratch, the slots or `out` (a call whose input overlaps
-        // the previous call's `out` is launched without the early start). The next call's HBM pass
-        // thus runs while this call waits for the other ranks, and at most two calls are in flight (a call's blocks
-        // cannot retire before the previous call completes), which the two slot parities cover.
+        // kernel launch as soon as it has started, and waits for the previous call's kernel to complete only after its
+        // own pass over the input, before it touches the scratch, the slots or `out` (a call whose input may have been
+        // written by a call still in flight is launched fully ordered: earlyStartAllowed). The next call's HBM pass
+        // thus runs while this call combines and waits for the other ranks. A call reaches its exchange only after the
+        // previous call has completed, so the exchanges of two calls never overlap and two slot parities suffice.
         template<typename T, int W, int ROp, int XOp, bool LOOP>
         __global__ void __launch_bounds__(kBlock) reduceAllRanksKernel(
             T const* __restrict__ in0,
@@ -649,7 +664,7 @@ namespace a3b
             cfg.dynamicSmemBytes = 0;
             cfg.stream = s;
             cfg.attrs = attr;
-            cfg.numAttrs = overlapsLastOut(props->ordinal, s, in0, in1, n * sizeof(T), out) ? 0 : 1;
+            cfg.numAttrs = earlyStartAllowed(props->ordinal, s, in0, in1, n * sizeof(T), out) ? 1 : 0;
             uint64_t const to = waitTimeoutNs();
             if(loop)
                 A3B_CUDA(cudaLaunchKernelEx(&cfg, reduceAllRanksKernel<T, W, ROp, XOp, true>, in0, in1, n, neutral, ppt,
@@ -754,7 +769,7 @@ namespace a3b
             cfg.blockDim = dim3(kBlock);
             cfg.stream = s;
             cfg.attrs = attr;
-            cfg.numAttrs = overlapsLastOut(props->ordinal, s, in0, in1, inBytes, out) ? 0 : 1;
+            cfg.numAttrs = earlyStartAllowed(props->ordinal, s, in0, in1, inBytes, out) ? 1 : 0;
             if(loop)
                 A3B_CUDA(cudaLaunchKernelEx(&cfg, reduceKernel<T, W, ROp, XOp, PITCHED, true, true>, in0, in1, n, rowLen,
                                             rowPitch, neutral, ppt, out, raw, w));
