@@ -115,6 +115,13 @@ def random_f32(out, seed, lo=-1.0, hi=1.0, start=0, stream=None):
 
 
 # -------------------------------------------------------------------------------------------------- reductions
+def set_early_start(enable=True, stream=None):
+    """Let the reductions on `stream` start while the previous kernel of the stream still runs (programmatic
+    dependent launch; off by default). Enable it only when no kernel on the stream signals its dependents early
+    (griddepcontrol.launch_dependents) before writing its output."""
+    capi.call("a3b_set_early_start", stream_handle(stream), 1 if enable else 0)
+
+
 def transform_reduce(neutral, out, reduce_fn, transform_fn, in0, in1=None, stream=None):
     """onHost::transformReduce(queue, neutral, out, reduceFn, transformFn, in0[, in1]); out: 1-element tensor."""
     code = dtype_code(in0)

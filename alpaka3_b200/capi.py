@@ -1,4 +1,5 @@
-"""ctypes binding of the C ABI declared in ``include/alpaka3_b200.h``.
+"""ctypes binding of the C ABI declared in ``include/alpaka3_b200.h`` (and the test hooks of
+``include/alpaka3_b200_testing.h``).
 
 This module only loads ``lib/libalpaka3_b200.so`` and declares the signatures; it has no fallback. If the library is
 missing, :func:`lib` raises :class:`LibraryNotBuilt` (run ``python -m alpaka3_b200.build`` or
@@ -55,6 +56,7 @@ SIGNATURES = {
     "a3b_transform_reduce_partial": [_P, _I, _I, _I, _P, _P, _U64, _P, _P],
     "a3b_transform_reduce_noalloc": [_P, _I, _I, _I, _P, _P, _U64, _P, _P],
     "a3b_reduce_2d": [_P, _I, _I, _P, _U64, _U64, _U64, _P, _P],
+    "a3b_set_early_start": [_P, _I],
     "a3b_ipc_handle_size": [],
     "a3b_peer_group_create": [_I, _I, _P, _P],
     "a3b_peer_group_connect": [_P, _P],
@@ -63,7 +65,6 @@ SIGNATURES = {
     "a3b_reduce_lower_ranks": [_P, _P, _I, _P, _U64, _P],
     "a3b_scan_buffer_size": [_I, _U64],
     "a3b_scan": [_P, _I, _I, _P, _P, _U64, _P, _P, ctypes.c_size_t],
-    "a3b_scan_debug_stall": [_P, _I, _P, _P, _U64, _U64],
     "a3b_nbody_update_velocities": [_P, _P, _P, _P, _P, _U64, _U64, _U64, _P, _P, _P, _F, _F],
     "a3b_nbody_step": [_P, _P, _P, _P, _P, _U64, _U64, _U64, _P, _P, _P, _F, _F],
     "a3b_heat_step": [_P, _P, _P, _U64, _U64, _U64, _U64, _U64, _D, _D],
@@ -75,6 +76,10 @@ SIGNATURES = {
     "a3b_halo_destroy": [_P],
     "a3b_heat_halo_publish": [_P, _P, _P, _U64, _U64, _U64],
     "a3b_heat_step_halo": [_P, _P, _P, _P, _U64, _U64, _U64, _D, _D],
+    # test hooks (include/alpaka3_b200_testing.h)
+    "a3b_scan_debug_stall": [_P, _I, _P, _P, _U64, _U64],
+    "a3b_debug_early_start_enable": [_I, _P, _I],
+    "a3b_debug_early_start_probe": [_I, _P, _P, _P, _U64, _P, _P],
 }
 _RESTYPES = {"a3b_last_error": ctypes.c_char_p, "a3b_scan_buffer_size": ctypes.c_size_t,
              "a3b_ipc_handle_size": ctypes.c_size_t, "a3b_halo_bytes": ctypes.c_size_t}

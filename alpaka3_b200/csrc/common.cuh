@@ -9,6 +9,7 @@
 #include <string>
 
 #include "alpaka3_b200.h"
+#include "alpaka3_b200_testing.h"
 
 #if defined(__CUDA_ARCH__) && (__CUDA_ARCH__ < 1000)
 #error "alpaka3_b200 is built for sm_100a (B200) only"

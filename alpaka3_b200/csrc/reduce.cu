@@ -18,12 +18,16 @@
 //     writes out[0]. Every ticket is reset by the block that drew the last number, so the scratch is left ready for
 //     the next call on the stream.
 // The combination order depends only on n: repeated runs, and runs on GPUs with other SM counts, give identical bits.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
 #include <cfloat>
 #include <climits>
 #include <mutex>
 #include <type_traits>
 
 #include <map>
+#include <set>
 #include <utility>
 #include <vector>
 
@@ -474,6 +478,11 @@ namespace a3b
                 writeResult<T, A>(out, total, rawPartial);
         }
 
+        // The early start is opt-in per (device, stream) (a3b_set_early_start): a reduction launched with it reads its
+        // input before griddepcontrol.wait, so a kernel just before it on the stream that signals its dependents early
+        // (griddepcontrol.launch_dependents) could still be writing that input. The caller who enables it asserts that
+        // no kernel on the stream does so; everything else is launched fully ordered.
+        //
         // Outputs of the reductions launched with the early start on each (device, stream) since the last one launched
         // fully ordered. Such a call may still be running while a later call of the stream reads its input (that read
         // comes before the later call's griddepcontrol.wait). A call whose input overlaps one of these outputs, or a
@@ -481,13 +490,33 @@ namespace a3b
         // launch starts only after all earlier work of the stream has completed.
         constexpr size_t kMaxEarly = 64;
         std::mutex gEarlyMutex;
+        std::set<std::pair<int, cudaStream_t>> gEarlyEnabled;
         std::map<std::pair<int, cudaStream_t>, std::vector<std::pair<uintptr_t, uintptr_t>>> gEarlyOutputs;
+
+        void setEarlyStart(int dev, cudaStream_t s, bool enable)
+        {
+            std::lock_guard<std::mutex> lock(gEarlyMutex);
+            auto const key = std::make_pair(dev, s);
+            if(enable)
+                gEarlyEnabled.insert(key);
+            else
+            {
+                gEarlyEnabled.erase(key);
+                gEarlyOutputs.erase(key);
+            }
+        }
 
         // true: launch with the early start; in both cases `out` (8 bytes) joins the stream's history
         bool earlyStartAllowed(int dev, cudaStream_t s, void const* in0, void const* in1, uint64_t inBytes, void* out)
         {
             std::lock_guard<std::mutex> lock(gEarlyMutex);
-            auto& h = gEarlyOutputs[std::make_pair(dev, s)];
+            auto const key = std::make_pair(dev, s);
+            if(!gEarlyEnabled.count(key))
+            {
+                gEarlyOutputs.erase(key); // fully ordered launches only: nothing can still run when the next call starts
+                return false;
+            }
+            auto& h = gEarlyOutputs[key];
             auto hit = [&](void const* p)
             {
                 if(!p)
@@ -928,26 +957,66 @@ namespace a3b
         __device__ __align__(256) unsigned char g_noAllocScratch[kNoAllocScratchBytes];
 
         std::mutex gNoAllocMutex;
-        void* gNoAllocAddress[64] = {};
+        struct NoAllocSlot
+        {
+            void* address;            // device address of g_noAllocScratch in the context below
+            unsigned long long ctxId; // driver id of the context that address belongs to (0: unknown)
+        };
+        NoAllocSlot gNoAllocSlots[64] = {};
+
+        // Driver id of the context current on this thread, 0 if there is none or it cannot be read. Context ids are
+        // unique for the life of the process, so a context re-created after cudaDeviceReset gets a new one.
+        unsigned long long currentContextId()
+        {
+            static PFN_cuCtxGetCurrent getCurrent = nullptr;
+            static PFN_cuCtxGetId getId = nullptr;
+            static std::once_flag once;
+            std::call_once(
+                once,
+                []
+                {
+                    cudaDriverEntryPointQueryResult q{};
+                    if(cudaGetDriverEntryPointByVersion("cuCtxGetCurrent", reinterpret_cast<void**>(&getCurrent), 4000,
+                                                        cudaEnableDefault, &q)
+                           != cudaSuccess
+                       || q != cudaDriverEntryPointSuccess)
+                        getCurrent = nullptr;
+                    if(cudaGetDriverEntryPointByVersion("cuCtxGetId", reinterpret_cast<void**>(&getId), 12000,
+                                                        cudaEnableDefault, &q)
+                           != cudaSuccess
+                       || q != cudaDriverEntryPointSuccess)
+                        getId = nullptr;
+                });
+            CUcontext ctx = nullptr;
+            unsigned long long id = 0;
+            if(!getCurrent || !getId || getCurrent(&ctx) != CUDA_SUCCESS || !ctx || getId(ctx, &id) != CUDA_SUCCESS)
+                return 0;
+            return id;
+        }
 
         // Device address of the static scratch for the current device. The array's name is a host-side stand-in,
-        // not a device address, so it is resolved once per device with cudaGetSymbolAddress (this first call must
-        // not happen inside a stream capture).
+        // not a device address, so it is resolved with cudaGetSymbolAddress once per device and context: on the
+        // first call on a device, and again when the device's context has been re-created (cudaDeviceReset unloads
+        // the module, so the array may sit at another address afterwards). Those calls must not happen inside a
+        // stream capture.
         int noAllocScratch(void** ptr)
         {
             int dev = 0;
             A3B_CUDA(cudaGetDevice(&dev));
             A3B_REQUIRE(dev >= 0 && dev < 64, "device ordinal out of range");
             std::lock_guard<std::mutex> lock(gNoAllocMutex);
-            if(!gNoAllocAddress[dev])
+            NoAllocSlot& slot = gNoAllocSlots[dev];
+            unsigned long long const ctx = currentContextId();
+            if(!slot.address || ctx == 0 || ctx != slot.ctxId)
             {
                 void* a = nullptr;
                 cudaError_t const e = cudaGetSymbolAddress(&a, g_noAllocScratch);
                 if(e != cudaSuccess)
                     return cudaFail(e, "cudaGetSymbolAddress(no-allocation scratch)");
-                gNoAllocAddress[dev] = a;
+                slot.address = a;
+                slot.ctxId = currentContextId(); // the lookup has made the device's context current
             }
-            *ptr = gNoAllocAddress[dev];
+            *ptr = slot.address;
             return A3B_OK;
         }
 
@@ -1068,6 +1137,28 @@ extern "C"
         A3B_REQUIRE(rows <= 1 || row_pitch_bytes >= row_len * static_cast<uint64_t>(es), "row pitch smaller than a row");
         return reduceEntry(stream, dtype, reduce_op, A3B_XFORM_IDENTITY, in, nullptr, rows, row_len, row_pitch_bytes,
                            neutral, out, false);
+    }
+
+    int a3b_set_early_start(a3b_stream_t stream, int enable)
+    {
+        int dev = 0;
+        A3B_CUDA(cudaGetDevice(&dev));
+        setEarlyStart(dev, static_cast<cudaStream_t>(stream), enable != 0);
+        return A3B_OK;
+    }
+
+    int a3b_debug_early_start_enable(int device, a3b_stream_t stream, int enable)
+    {
+        setEarlyStart(device, static_cast<cudaStream_t>(stream), enable != 0);
+        return A3B_OK;
+    }
+
+    int a3b_debug_early_start_probe(int device, a3b_stream_t stream, void const* in0, void const* in1,
+                                    uint64_t in_bytes, void* out, int* early)
+    {
+        A3B_REQUIRE(early, "null result pointer");
+        *early = earlyStartAllowed(device, static_cast<cudaStream_t>(stream), in0, in1, in_bytes, out) ? 1 : 0;
+        return A3B_OK;
     }
 
     int a3b_transform_reduce_noalloc(a3b_stream_t stream, int dtype, int reduce_op, int transform_op, void const* in0,

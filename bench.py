@@ -30,8 +30,19 @@ sys.path.insert(0, ROOT)
 METRIC = "triad/dot/reduce/scan HBM GB/s (fraction of ~8 TB/s) at 1/2/4/8 B200"
 N_SUMSQ = 1 << 30
 SEED = 0x5EED0001
+# the same string in both arms; how each arm splits the work is in config.parallelism
 WORKLOAD = ("transformReduce sum of squares (std::plus, x*x) over 2^30 fp32 uniform[-1,1) from a seeded Philox "
-            "stream, contiguous shards per rank, fp64 partials combined across ranks")
+            "stream")
+FP32_PEAK = 148 * 128 * 2 * 1.965e9  # FP32 lanes x 2 flop x boost clock, nominal (not driver-measured)
+
+
+def host_threads():
+    """Host threads this process may run on (the OpenMP thread count of the CPU arms; launchers such as torchrun set
+    OMP_NUM_THREADS=1, which must not decide the reference's core count)."""
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
 
 
 def peaks():
@@ -149,6 +160,8 @@ def run_b200(args):
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     capi.lib()
+    # nothing on this stream signals its dependents early, so consecutive reductions may overlap
+    algo.set_early_start(True)
     peak, peak_kind = peaks()
 
     # ---------------------------------------------------------------- headline: sum of squares, 2^30 fp32
@@ -233,10 +246,18 @@ def run_b200(args):
                "path": "a3b_memcpy_async(H2D, pinned) + a3b_transform_reduce + a3b_memcpy_async(D2H)"}
         del host
 
-    # ---------------------------------------------------------------- other kernels of the metric (N = 1)
+    # ---------------------------------------------------------------- other kernels of the metric
+    del x
+    torch.cuda.empty_cache()
     parts = None
-    if world == 1 and not args.no_parts:
-        parts = bench_parts(torch, algo, dev, args, peak)
+    if not args.no_parts:
+        if world == 1:
+            parts = bench_parts(torch, algo, dev, args, peak)
+        else:
+            parts = bench_parts_multi(torch, algo, adist, world, rank, dev, args, peak, peak_kind)
+
+    # ---------------------------------------------------------------- parity of every sharded path (small sizes)
+    parity = None if args.no_parity else parity_checks(torch, algo, adist, world, rank, dev)
 
     # ---------------------------------------------------------------- CPU baseline: alpaka3's OpenMP backend
     cpu = None
@@ -250,8 +271,11 @@ def run_b200(args):
             "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded Philox4x32-10, uniform [-1,1))",
             "config": {"workload": WORKLOAD, "n": N_SUMSQ, "bytes_per_step": int(total_bytes),
                        "per_rank_elements": n_local, "l2": "inputs larger than L2 (4.29 GB total, >= 537 MB per GPU)",
-                       "parallelism": (f"shard{world}+fused peer all-reduce" if group is not None else
-                                       f"shard{world}+NCCL all-reduce") if dist_on else "single GPU"},
+                       "parallelism": (f"contiguous shards on {world} GPUs, fp64 partials combined by a fused peer "
+                                       "all-reduce" if group is not None else
+                                       f"contiguous shards on {world} GPUs, fp64 partials combined by NCCL all-reduce")
+                       if dist_on else "single GPU",
+                       "early_start": "consecutive reductions overlap (a3b_set_early_start on the bench stream)"},
             "result": result,
             "roofline": {"bound": "hbm", "achieved": round(kern_gbs, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(kern_gbs / peak, 4), "peak_kind": peak_kind,
@@ -266,6 +290,8 @@ def run_b200(args):
             line["cpu_baseline"] = cpu
         if parts:
             line["parts"] = parts
+        if parity is not None:
+            line["parity"] = parity
         print(json.dumps(line), flush=True)
     if dist_on:
         import torch.distributed as dist
@@ -379,6 +405,7 @@ def cpu_baseline(budget_s=8.0, n=1 << 28):
         ref, port = Ref(), Port()
     except Exception as e:  # noqa: BLE001
         return {"value": None, "unit": "GB/s", "kind": "reference", "unavailable": str(e)}
+    ref.set_num_threads(host_threads())
     x = port.gen_f32(n, -1.0, 1.0, seed=SEED)
     ref.sumsq(x)  # warm-up
     times = []
@@ -405,6 +432,7 @@ def run_reference(args):
     except Exception as e:  # noqa: BLE001
         print(json.dumps({"impl": "reference", "unavailable": f"alpaka3 host backend not built: {e}"}), flush=True)
         return
+    ref.set_num_threads(host_threads())
     x = port.gen_f32(N_SUMSQ, -1.0, 1.0, seed=SEED)
     for _ in range(args.warmup):
         ref.sumsq(x)
@@ -421,9 +449,8 @@ def run_reference(args):
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 3), "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic (seeded Philox4x32-10, uniform [-1,1))",
-        "config": {"workload": WORKLOAD.replace(", contiguous shards per rank, fp64 partials combined across ranks",
-                                                "") + ", whole input on the host", "n": N_SUMSQ,
-                   "bytes_per_step": 4 * N_SUMSQ, "parallelism": "host OpenMP"},
+        "config": {"workload": WORKLOAD, "n": N_SUMSQ, "bytes_per_step": 4 * N_SUMSQ,
+                   "parallelism": f"alpaka3 exec::cpuOmpBlocks, {cores} OpenMP threads, whole input in host memory"},
         "result": float(r),
         "cpu_baseline": {"value": round(value, 2), "unit": "GB/s", "cores": cores, "kind": "reference",
                          "sample": "alpaka3 onHost::transformReduce(exec::cpuOmpBlocks) over the full 2^30 fp32 "
@@ -486,39 +513,34 @@ def run_profile_case(args):
     print(json.dumps({"profile_case": case, "n_log2": lg, "kernel_ms": kern, "units_per_s": nbytes / (kern * 1e-3)}))
 
 
-def run_workload(args):
-    """The other configurations of the metric on N ranks (one JSON line from rank 0, same keys as the headline):
-    triad / dot (BabelStream fp64, 2^25 elements per array PER GPU: weak scaling, so every rank's arrays exceed L2),
-    scan_i32 (exclusive scan of 2^30 int32 split across ranks, reduce + all-gather of totals + carried scan),
-    scan_u64 (inclusive scan of 2^28 uint64, likewise), nbody (262144 bodies split across ranks, all-gather of
-    positions each step), heat (32768^2 grid in row slabs, halo rows exchanged each step, overlapped)."""
-    import torch
-    from alpaka3_b200 import algo, dist as adist
-    world, rank, local = adist.init()
+def setup_workload(torch, algo, adist, wl, world, rank, dev, collective="fused"):
+    """One of the metric's other configurations on N ranks: returns a namespace with the step function, this rank's
+    and the whole job's units per step, a description and a close() for its peer resources.
+    triad / dot: BabelStream fp64, 2^25 elements per array PER GPU (weak scaling, every rank's arrays exceed L2);
+    scan_i32 / scan_u64: exclusive scan of 2^30 int32 / inclusive scan of 2^28 uint64 split across ranks (one fused
+    launch for the shard total and the carry over lower ranks via peer slots, then the carried single-pass scan);
+    nbody: 262144 bodies split across ranks, positions all-gathered every step; heat: 32768^2 fp64 in row slabs, one
+    halo row exchanged with each neighbour per step inside the stencil kernel (or by NCCL)."""
+    import types
     dist_on = world > 1
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
-    peak, peak_kind = peaks()
-    wl = args.workload
-    s = torch.cuda.current_stream()
-    launches = [0]
-    scaling = "strong"
+    W = types.SimpleNamespace(name=wl, scaling="strong", unit="GB/s", close=lambda: None)
     if wl in ("triad", "dot"):
         n = 1 << 25
         a, b, c = (torch.empty(n, dtype=torch.float64, device=dev) for _ in range(3))
         algo.babelstream("init", a, b, c)
         out = torch.empty(1, dtype=torch.float64, device=dev)
-        scaling = "weak"
+        W.scaling, W.dtype = "weak", "f64"
         if wl == "triad":
-            fn, unit_bytes = (lambda: algo.babelstream("triad", a, b, c)), 24.0 * n
+            W.fn, W.unit_bytes = (lambda: algo.babelstream("triad", a, b, c)), 24.0 * n
         else:
-            group = adist.PeerGroup() if dist_on else None  # noqa: F841 - closed after the timing
-            fn = (lambda: group.transform_reduce(0.0, "plus", "product", a, b, out=out)) if group else (
+            group = adist.PeerGroup() if dist_on else None
+            W.fn = (lambda: group.transform_reduce(0.0, "plus", "product", a, b, out=out)) if group else (
                 lambda: algo.transform_reduce(0.0, out, "plus", "product", a, b))
-            unit_bytes = 16.0 * n
-        total = unit_bytes * world
-        desc = f"BabelStream {wl} fp64, 2^25 elements per array on each GPU (weak scaling)"
-        metric_unit = "GB/s"
+            W.unit_bytes = 16.0 * n
+            if group:
+                W.close = group.close
+        W.total = W.unit_bytes * world
+        W.desc = f"BabelStream {wl} fp64, 2^25 elements per array on each GPU (weak scaling)"
     elif wl in ("scan_i32", "scan_u64"):
         n = (1 << 30) if wl == "scan_i32" else (1 << 28)
         dt = torch.int32 if wl == "scan_i32" else torch.int64
@@ -529,15 +551,17 @@ def run_workload(args):
         else:
             algo.random_u64(x, SEED, start=b0)
         y = torch.empty_like(x)
-        group = adist.PeerGroup() if dist_on else None  # noqa: F841 - closed after the timing
+        group = adist.PeerGroup() if dist_on else None
         incl = wl != "scan_i32"
-        fn = (lambda: group.scan(incl, y, x)) if group else (lambda: algo._scan(incl, y, x))
-        unit_bytes = 2.0 * x.element_size() * (e0 - b0)
-        total = 2.0 * x.element_size() * n
-        desc = (f"{'exclusive' if wl == 'scan_i32' else 'inclusive'} scan of 2^{30 if wl == 'scan_i32' else 28} "
-                f"{'int32 in [0,16)' if wl == 'scan_i32' else 'uint64'} split across ranks (one fused launch for the "
-                "shard total and the carry over lower ranks via peer slots, then the carried single-pass scan)")
-        metric_unit = "GB/s"
+        W.fn = (lambda: group.scan(incl, y, x)) if group else (lambda: algo._scan(incl, y, x))
+        if group:
+            W.close = group.close
+        W.unit_bytes = 2.0 * x.element_size() * (e0 - b0)
+        W.total = 2.0 * x.element_size() * n
+        W.dtype = "int32" if wl == "scan_i32" else "uint64"
+        W.desc = (f"{'exclusive' if wl == 'scan_i32' else 'inclusive'} scan of 2^{30 if wl == 'scan_i32' else 28} "
+                  f"{'int32 in [0,16)' if wl == 'scan_i32' else 'uint64'} split across ranks (one fused launch for "
+                  "the shard total and the carry over lower ranks via peer slots, then the carried single-pass scan)")
     elif wl == "nbody":
         nb = 262144
         m, px, py, pz = (torch.empty(nb, dtype=torch.float32, device=dev) for _ in range(4))
@@ -547,11 +571,11 @@ def run_workload(args):
         b0, e0 = adist.shard_range(nb, rank, world)
         v = [torch.zeros(e0 - b0, dtype=torch.float32, device=dev) for _ in range(3)]
         sim = adist.NBody(m, px, py, pz, *v, b0)
-        fn = lambda: sim.step(1e-3, 1e-3)  # noqa: E731
-        unit_bytes = 20.0 * (e0 - b0) * nb
-        total = 20.0 * nb * nb + 6.0 * nb
-        desc = "all-pairs nBody, 262144 fp32 bodies split across ranks, positions all-gathered every step"
-        metric_unit = "GFLOP/s"
+        W.fn = lambda: sim.step(1e-3, 1e-3)
+        W.unit_bytes = 20.0 * (e0 - b0) * nb
+        W.total = 20.0 * nb * nb + 6.0 * nb
+        W.unit, W.dtype = "GFLOP/s", "f32"
+        W.desc = "all-pairs nBody, 262144 fp32 bodies split across ranks, positions all-gathered every step"
     else:
         side = 32768
         hb, he = adist.shard_range(side, rank, world)
@@ -559,59 +583,199 @@ def run_workload(args):
         dx = 1.0 / (side + 1)
         algo.heat_init(u, dx, dx, row_offset=hb, global_rows=side)
         w = u.clone()
-        slab = adist.HeatSlab(u, w, 0.2, 0.2, collective=args.collective)
-        fn = slab.step
-        unit_bytes = 16.0 * (he - hb) * side
-        total = 16.0 * side * side
-        desc = ("heat 5-point stencil, 32768^2 fp64 in row slabs, one halo row exchanged with each neighbour per step "
-                + ("(one kernel per step: boundary rows stored into the neighbours' mailboxes over NVLink)"
-                   if args.collective == "fused" else "(NCCL send/recv overlapped with the interior update)"))
-        metric_unit = "GB/s"
+        slab = adist.HeatSlab(u, w, 0.2, 0.2, collective=collective)
+        W.fn = slab.step
+        W.close = slab.close
+        W.unit_bytes = 16.0 * (he - hb) * side
+        W.total = 16.0 * side * side
+        W.dtype = "f64"
+        W.desc = ("heat 5-point stencil, 32768^2 fp64 in row slabs, one halo row exchanged with each neighbour per "
+                  "step " + ("(one kernel per step: boundary rows stored into the neighbours' mailboxes over NVLink)"
+                             if collective == "fused" else "(NCCL send/recv overlapped with the interior update)"))
+    return W
+
+
+def time_workload(torch, dist_on, W, steps, warmup, peak, peak_kind):
+    """Times W.fn: K steps back to back (value) and K steps with an event pair each (the per-step duration for the
+    roofline), max over ranks; returns the whole-job value, ms per step and the roofline entry."""
+    s = torch.cuda.current_stream()
+    launches = [0]
 
     def step(ev):
         if ev:
             ev[0].record(s)
-        fn()
+        W.fn()
         if ev:
             ev[1].record(s)
             launches[0] += 1
 
-    sampler = ClockSampler(pci_bus_id(torch, local))
-    sampler.start()
-    ms, _ = time_steps(torch, dist_on, step, args.steps, args.warmup, kernel_events=False)  # value: back to back
-    _, kern = time_steps(torch, dist_on, step, args.steps, args.warmup)  # per-step events: the roofline's duration
-    sampler.stop()
-    if wl == "heat":
-        slab.close()
+    ms, _ = time_steps(torch, dist_on, step, steps, warmup, kernel_events=False)
+    _, kern = time_steps(torch, dist_on, step, steps, warmup)
     ms = max_over_ranks(torch, dist_on, ms)
     kern = max_over_ranks(torch, dist_on, kern)
-    scale = 1e9
-    value = total / (ms * 1e-3) / scale
-    per_gpu = unit_bytes / (kern * 1e-3) / scale
-    if metric_unit == "GFLOP/s":
-        fp32_peak = 148 * 128 * 2 * 1.965e9 / 1e9
+    value = W.total / (ms * 1e-3) / 1e9
+    per_gpu = W.unit_bytes / (kern * 1e-3) / 1e9
+    if W.unit == "GFLOP/s":
+        fp32_peak = FP32_PEAK / 1e9
         roof = {"bound": "fp32 pipe", "achieved": round(per_gpu, 1), "peak": round(fp32_peak, 1), "unit": "GFLOP/s",
                 "frac": round(per_gpu / fp32_peak, 4), "peak_kind": "nominal (148 SMs x 128 lanes x 2 x 1.965 GHz)"}
     else:
         roof = {"bound": "hbm", "achieved": round(per_gpu, 1), "peak": peak, "unit": "GB/s",
                 "frac": round(per_gpu / peak, 4), "peak_kind": peak_kind}
     roof["step_ms_per_rank"] = round(kern, 5)
+    return value, ms, roof, launches[0]
+
+
+def run_workload(args):
+    """The other configurations of the metric on N ranks (one JSON line from rank 0, same keys as the headline)."""
+    import torch
+    from alpaka3_b200 import algo, dist as adist
+    world, rank, local = adist.init()
+    dist_on = world > 1
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    algo.set_early_start(True)
+    peak, peak_kind = peaks()
+    W = setup_workload(torch, algo, adist, args.workload, world, rank, dev, args.collective)
+    sampler = ClockSampler(pci_bus_id(torch, local))
+    sampler.start()
+    value, ms, roof, launches = time_workload(torch, dist_on, W, args.steps, args.warmup, peak, peak_kind)
+    sampler.stop()
+    W.close()
     if rank == 0:
-        line = {"metric": METRIC, "value": round(value, 2), "unit": metric_unit, "n_gpus": world, "steps": args.steps,
-                "warmup": args.warmup, "ms_per_step": round(ms, 5), "higher_is_better": True, "scaling": scaling,
-                "vs_baseline": None, "dtype": {"triad": "f64", "dot": "f64", "scan_i32": "int32", "scan_u64": "uint64",
-                                               "nbody": "f32", "heat": "f64"}[wl],
-                "data": "synthetic (seeded Philox4x32-10)", "config": {"workload": desc, "name": wl},
-                "roofline": roof, "gpu_launches": launches[0], "clocks": sampler.summary()}
+        line = {"metric": METRIC, "value": round(value, 2), "unit": W.unit, "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": round(ms, 5), "higher_is_better": True, "scaling": W.scaling,
+                "vs_baseline": None, "dtype": W.dtype, "data": "synthetic (seeded Philox4x32-10)",
+                "config": {"workload": W.desc, "name": args.workload}, "roofline": roof, "gpu_launches": launches,
+                "clocks": sampler.summary()}
         print(json.dumps(line), flush=True)
     if dist_on:
         import torch.distributed as dist
         torch.cuda.synchronize()
         dist.barrier()
-        if wl in ("dot", "scan_i32", "scan_u64") and group is not None:
-            group.close()
-        dist.barrier()
         dist.destroy_process_group()
+
+
+def bench_parts_multi(torch, algo, adist, world, rank, dev, args, peak, peak_kind):
+    """N > 1: the metric's other configurations sharded over the same ranks (max-over-ranks device time)."""
+    parts = {}
+    dist_on = world > 1
+    for wl in ("triad", "dot", "scan_i32", "scan_u64", "nbody", "heat"):
+        W = setup_workload(torch, algo, adist, wl, world, rank, dev, args.collective)
+        steps = 10 if wl == "nbody" else max(args.steps, 20)
+        value, ms, roof, _ = time_workload(torch, dist_on, W, steps, max(args.warmup, 3), peak, peak_kind)
+        W.close()
+        parts[wl] = {W.unit: round(value, 1), "ms_per_step": round(ms, 5), "scaling": W.scaling,
+                     "per_gpu_frac": roof["frac"], "per_gpu_achieved": roof["achieved"], "workload": W.desc}
+        del W
+        torch.cuda.synchronize()
+        torch.cuda.empty_cache()
+    return parts
+
+
+def parity_checks(torch, algo, adist, world, rank, dev):
+    """Small-size parity of every sharded path on these ranks, outside the timed region, against independent torch
+    references computed on each rank for the whole (small) problem: the fused reduce + all-reduce (fp64 sum, rel
+    1e-5), the peer-carried exclusive int32 scan with wrap-around and the inclusive uint64 scan (torch cumsum,
+    bit-exact), the nBody step with the all-gather (fp64 all-pairs, rel 1e-4 normwise) and the heat step with the
+    fused halo exchange (the same operation order in torch, bit-exact). Returns {check: true/false over all ranks}."""
+    res = {}
+    group = adist.PeerGroup() if world > 1 else None
+    try:
+        # transformReduce sum of squares, fp32 shards, fused peer all-reduce
+        n = (1 << 24) + 5
+        full = torch.empty(n, dtype=torch.float32, device=dev)
+        algo.random_f32(full, SEED, -1.0, 1.0)
+        b, e = adist.shard_range(n, rank, world)
+        x = full[b:e].clone()
+        out = torch.empty(1, dtype=torch.float32, device=dev)
+        if group:
+            group.transform_reduce(0.0, "plus", "square", x, out=out)
+        else:
+            algo.transform_reduce(0.0, out, "plus", "square", x)
+        exact = float((full.double() ** 2).sum().item())
+        res["reduce_sumsq_rel_le_1e-5"] = abs(float(out.item()) - exact) / exact <= 1e-5
+        # exclusive int32 scan, values that make the carry wrap
+        xs_full = torch.empty(n, dtype=torch.int32, device=dev)
+        algo.random_u32(xs_full, SEED, shift=1)
+        xs = xs_full[b:e].clone()
+        ys = torch.empty_like(xs)
+        if group:
+            group.scan(False, ys, xs)
+        else:
+            algo.exclusive_scan(ys, xs)
+        want = (torch.cumsum(xs_full.long(), 0) - xs_full.long()).to(torch.int32)[b:e]
+        res["scan_i32_exclusive_bit_exact"] = bool(torch.equal(ys, want))
+        # inclusive uint64 scan (int64 storage, wrapping adds)
+        n64 = (1 << 22) + 3
+        xu_full = torch.empty(n64, dtype=torch.int64, device=dev)
+        algo.random_u64(xu_full, SEED)
+        b6, e6 = adist.shard_range(n64, rank, world)
+        xu = xu_full[b6:e6].clone()
+        yu = torch.empty_like(xu)
+        if group:
+            group.scan(True, yu, xu)
+        else:
+            algo.inclusive_scan(yu, xu)
+        res["scan_u64_inclusive_bit_exact"] = bool(torch.equal(yu, torch.cumsum(xu_full, 0)[b6:e6]))
+        del full, x, xs_full, xs, ys, want, xu_full, xu, yu
+    finally:
+        if group:
+            torch.cuda.synchronize()
+            group.close()
+
+    # nBody: 4096 bodies split across ranks, 3 kick + drift steps with the all-gather, against fp64 all-pairs
+    nb, steps, dt, eps = 4096, 3, 1e-3, 1e-3
+    m = torch.empty(nb, dtype=torch.float32, device=dev)
+    algo.random_f32(m, SEED + 1, 0.5, 1.0)
+    pos = [torch.empty(nb, dtype=torch.float32, device=dev) for _ in range(3)]
+    for k, t in enumerate(pos):
+        algo.random_f32(t, SEED + 2 + k, 0.0, 1.0)
+    P = torch.stack([t.double() for t in pos], 1)
+    V = torch.zeros_like(P)
+    M = m.double()
+    for _ in range(steps):
+        d = P[None, :, :] - P[:, None, :]
+        r2 = (d * d).sum(-1) + eps
+        a = ((M[None, :] / torch.sqrt(r2 ** 3))[:, :, None] * d).sum(1)
+        V = V + a * dt
+        P = P + V * dt
+    bb, eb = adist.shard_range(nb, rank, world)
+    v = [torch.zeros(eb - bb, dtype=torch.float32, device=dev) for _ in range(3)]
+    sim = adist.NBody(m, *pos, *v, bb)
+    for _ in range(steps):
+        sim.step(dt, eps)
+    torch.cuda.synchronize()
+    got = torch.stack([t.double() for t in pos], 1)
+    res["nbody_positions_rel_le_1e-4"] = float((got - P).abs().max() / P.abs().max()) <= 1e-4
+
+    # heat: 1000 x 1000 interior, 7 steps, row slabs with the fused halo exchange, bit-exact
+    nh, hsteps, r = 1000, 7, 0.2
+    dx = 1.0 / (nh + 1)
+    u = torch.zeros((nh + 2, nh + 2), dtype=torch.float64, device=dev)
+    algo.heat_init(u, dx, dx)
+    ref = u.clone()
+    for _ in range(hsteps):
+        c = ref[1:-1, 1:-1]
+        nxt = ref.clone()
+        nxt[1:-1, 1:-1] = (c * (1.0 - 2.0 * r - 2.0 * r) + ref[1:-1, :-2] * r + ref[1:-1, 2:] * r
+                           + ref[:-2, 1:-1] * r + ref[2:, 1:-1] * r)
+        ref = nxt
+    hb, he = adist.shard_range(nh, rank, world)
+    cur = u[hb:he + 2].clone()
+    slab = adist.HeatSlab(cur, cur.clone(), r, r)
+    for _ in range(hsteps):
+        slab.step()
+    slab.close()
+    torch.cuda.synchronize()
+    res["heat_fused_halo_bit_exact"] = bool(torch.equal(slab.cur[1:he - hb + 1], ref[hb + 1:he + 1]))
+
+    if world > 1:
+        import torch.distributed as dist
+        allres = [None] * world
+        dist.all_gather_object(allres, res)
+        res = {k: all(r[k] for r in allres) for k in res}
+    return res
 
 
 def main():
@@ -623,6 +787,7 @@ def main():
     ap.add_argument("--no-parts", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-parity", action="store_true", help="skip the small-size parity checks of the sharded paths")
     ap.add_argument("--cpu-seconds", type=float, default=8.0)
     ap.add_argument("--workload", default="sumsq",
                     choices=["sumsq", "triad", "dot", "scan_i32", "scan_u64", "nbody", "heat"],

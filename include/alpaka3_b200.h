@@ -157,30 +157,50 @@ A3B_API int a3b_random_f32(a3b_stream_t stream, float* out, uint64_t n, uint64_t
  * out: device pointer to ONE element of dtype, written with the final value (no pre-fill launch needed).
  * neutral: host pointer to one element of dtype. One launch; the final combination runs in the last block in a fixed
  * order, so a given (device, n) always gives the same bits. fp32 inputs are accumulated in fp64 inside the kernel;
- * integer + wraps (two's complement). */
+ * integer + wraps (two's complement).
+ * Ordering: by default the launch is fully ordered after all earlier work of the stream. With a3b_set_early_start
+ * enabled on the stream it may start while the previous kernel of the stream still runs (see there). */
 A3B_API int a3b_transform_reduce(a3b_stream_t stream, int dtype, int reduce_op, int transform_op, void const* in0,
                          void const* in1, uint64_t n, void const* neutral, void* out);
 
 /* Same, but the per-block partials are left as fp64 (float dtypes) / 64-bit integers in partial_out[0] instead of
- * being rounded to dtype: used to combine shards across GPUs before the final rounding. */
+ * being rounded to dtype: used to combine shards across GPUs before the final rounding. Ordering as
+ * a3b_transform_reduce. */
 A3B_API int a3b_transform_reduce_partial(a3b_stream_t stream, int dtype, int reduce_op, int transform_op, void const* in0,
                                  void const* in1, uint64_t n, void const* neutral, void* partial_out);
 
 /* No counterpart in the reference: a3b_transform_reduce for callers that cannot allocate device memory -- a process
  * whose device memory is owned by another allocator's pool, a service that must keep a fixed, accounted memory
- * footprint, a latency-critical loop that cannot afford an allocation's implicit synchronisation. Same arguments and result
- * as a3b_transform_reduce over a dense 1-D input; it allocates nothing. Its scratch is one fixed 16 KB static device
- * array per GPU that loads the library (held until the process exits): the tickets and partials of at most 2024 blocks,
- * each of which takes several chunks of a large input (A3B_ERR_TOO_LARGE is kept for a layout that would not fit). The first
- * call on a device looks up that array's device address, so make the first call before any stream capture. All
- * calls share the array: calls that overlap on the GPU (different streams, devices' own streams in parallel) race
- * and must be serialised by the caller. */
+ * footprint, a latency-critical loop that cannot afford an allocation's implicit synchronisation. Same arguments as
+ * a3b_transform_reduce over a dense 1-D input; it allocates nothing. The result is the same for integer data; for
+ * floating-point data it agrees within rounding (its grid is capped at 2024 blocks, so above that size the partials
+ * are combined in another order) and is deterministic for a given n. Its scratch is one fixed 16 KB static device
+ * array per GPU that loads the library (held until the process exits): the tickets and partials of at most 2024
+ * blocks, each of which takes several chunks of a large input (A3B_ERR_TOO_LARGE is kept for a layout that would not
+ * fit). The first call on a device (and the first after the device's context was re-created, e.g. by
+ * cudaDeviceReset) looks up that array's device address, so make that call before any stream capture. All calls
+ * share the array: calls that overlap on the GPU (different streams, devices' own streams in parallel) race and must
+ * be serialised by the caller. Always launched fully ordered. */
 A3B_API int a3b_transform_reduce_noalloc(a3b_stream_t stream, int dtype, int reduce_op, int transform_op,
                                          void const* in0, void const* in1, uint64_t n, void const* neutral, void* out);
 
+/* Early start of the reductions on `stream` of the current device (a3b_transform_reduce, _partial, a3b_reduce_2d,
+ * a3b_transform_reduce_allranks, a3b_reduce_lower_ranks); off by default. No counterpart in alpaka3, whose kernels
+ * are plain launches. When enabled, a reduction is launched with programmatic dependent launch: it starts as soon as
+ * the previous kernel of the stream lets its dependents launch, reads its input, and waits for that kernel to
+ * complete only before it touches its scratch or `out`. The next call thus streams its input while this one combines
+ * (and, across ranks, waits for its peers). The library launches fully ordered any call whose input overlaps the
+ * output of one of its own reductions that may still run (every reduction started early since the last fully ordered
+ * launch). ENABLE IT ONLY IF no other kernel on the stream executes griddepcontrol.launch_dependents
+ * (cudaTriggerProgrammaticLaunchCompletion) before its output is written -- e.g. kernels built with programmatic
+ * dependent launch by CUTLASS or some cuBLASLt kernels: the reduction could read that output before it is written.
+ * Copies, memsets and kernels without that instruction are always complete before the reduction reads its input. */
+A3B_API int a3b_set_early_start(a3b_stream_t stream, int enable);
+
 /* onHost::reduce(queue, neutral, out, reduceFn, in) (include/alpaka/onHost/algo/reduce.hpp:28-79) over a pitched
  * 2-D view: `rows` rows of `row_len` elements, consecutive rows `row_pitch_bytes` apart (rows = 1 for 1-D data).
- * N-D alpaka buffers whose slower dimensions are dense multiples of the row pitch map onto this form. */
+ * N-D alpaka buffers whose slower dimensions are dense multiples of the row pitch map onto this form. Ordering as
+ * a3b_transform_reduce. */
 A3B_API int a3b_reduce_2d(a3b_stream_t stream, int dtype, int reduce_op, void const* in, uint64_t rows, uint64_t row_len,
                   uint64_t row_pitch_bytes, void const* neutral, void* out);
 
@@ -201,10 +221,9 @@ A3B_API int a3b_peer_group_destroy(a3b_peer_group* group);
  * per rank reduces the local shard, its last block stores the unrounded partial into every rank's slot (peer stores
  * over NVLink), waits (bounded) for all ranks' partials and combines them in rank order, so every rank writes the
  * same bits to its `out`. All ranks must make the same sequence of calls. A wait that runs out sets bit 0 of the
- * device error word (a3b_get_device_error). Consecutive calls on one stream overlap (programmatic dependent launch):
- * a call reads its input while the previous call still waits for the other ranks, and touches its scratch, the slots
- * and `out` only after that call has completed. A call whose input overlaps the previous call's `out` is launched
- * fully ordered instead; input written by any other kernel or copy is always complete before the call reads it. */
+ * device error word (a3b_get_device_error). Ordering as a3b_transform_reduce: with a3b_set_early_start enabled on the
+ * stream, consecutive calls overlap, so a call reads its input while the previous call still waits for the other
+ * ranks. */
 A3B_API int a3b_transform_reduce_allranks(a3b_stream_t stream, a3b_peer_group* group, int dtype, int reduce_op,
                                           int transform_op, void const* in0, void const* in1, uint64_t n,
                                           void const* neutral, void* out);
@@ -230,11 +249,6 @@ A3B_API size_t a3b_scan_buffer_size(int dtype, uint64_t n);
  *         scan is split across GPUs); null means 0. Integer arithmetic wraps (two's complement). */
 A3B_API int a3b_scan(a3b_stream_t stream, int dtype, int inclusive, void const* in, void* out, uint64_t n,
              void const* carry_in, void* buffer, size_t buffer_bytes);
-
-/* Failure-detection test hook: runs a3b_scan (no caller buffer) with tile `stall_tile` never publishing its aggregate,
- * so every later tile's bounded wait for it gives up after the configured timeout, raises bit 0 of the device error
- * word and returns. The output is undefined; the context stays usable. */
-A3B_API int a3b_scan_debug_stall(a3b_stream_t stream, int dtype, void const* in, void* out, uint64_t n, uint64_t stall_tile);
 
 /* ----------------------------------------------------------------------------------------------------- nBody */
 

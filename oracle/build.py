@@ -15,7 +15,8 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 ORACLE_SO = os.path.join(HERE, "liboracle.so")
 REF_SO = os.path.join(HERE, "_ref", "libalpaka_ref.so")
 REF_CUDA_BENCH = os.path.join(HERE, "_ref", "ref_cuda_bench")
-REFERENCE_ROOT = os.environ.get("ALPAKA_REFERENCE_ROOT", "/root/reference")
+# where the alpaka3 source tree lies; the build script passes it explicitly (no default: without it, _ref is not built)
+REFERENCE_ROOT = os.environ.get("ALPAKA_REFERENCE_ROOT")
 
 
 def _stale(target, sources):
@@ -35,16 +36,20 @@ def build_oracle(force=False):
     return ORACLE_SO
 
 
-def build_ref(force=False):
-    if not os.path.isdir(os.path.join(REFERENCE_ROOT, "include", "alpaka")):
+def build_ref(force=False, reference_root=None):
+    """Builds oracle/_ref from the alpaka3 tree at `reference_root` (or $ALPAKA_REFERENCE_ROOT); without one, or
+    where it does not exist, keeps whatever was built before."""
+    root = reference_root or REFERENCE_ROOT
+    if not root or not os.path.isdir(os.path.join(root, "include", "alpaka")):
         return REF_SO if os.path.exists(REF_SO) else None
     srcs = [os.path.join(HERE, f) for f in ("ref_harness.cpp", "ref_ops.hpp", "ref_cuda_bench.cpp", "build_ref.sh")]
     if force or _stale(REF_SO, srcs) or _stale(REF_CUDA_BENCH, srcs):
-        subprocess.check_call(["bash", os.path.join(HERE, "build_ref.sh"), REFERENCE_ROOT])
+        subprocess.check_call(["bash", os.path.join(HERE, "build_ref.sh"), root])
     return REF_SO
 
 
 if __name__ == "__main__":
     force = "--force" in sys.argv
+    roots = [a for a in sys.argv[1:] if not a.startswith("--")]
     print(build_oracle(force))
-    print(build_ref(force))
+    print(build_ref(force, roots[0] if roots else None))

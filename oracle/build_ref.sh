@@ -2,11 +2,11 @@
 # Builds oracle/_ref/libalpaka_ref.so: the reference's own host backend (alpaka3 headers, unmodified, read in place)
 # behind the C entry points of oracle/ref_harness.cpp. Test infrastructure only.
 #
-# usage: oracle/build_ref.sh [REFERENCE_ROOT]   (default /root/reference)
+# usage: oracle/build_ref.sh REFERENCE_ROOT   (the alpaka3 source tree)
 # FP contraction is pinned off so element-wise results are IEEE-exact per operation (the CUDA kernels use the
 # same explicitly rounded _rn operations), which makes copy/mul/add/triad bit-comparable.
 set -euo pipefail
-REF="${1:-/root/reference}"
+REF="${1:?usage: build_ref.sh REFERENCE_ROOT}"
 HERE="$(cd "$(dirname "$0")" && pwd)"
 OUT="$HERE/_ref"
 mkdir -p "$OUT"

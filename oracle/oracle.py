@@ -187,6 +187,11 @@ class Ref:
         L.ref_heat_problem.argtypes = [ctypes.c_int, _U32, _U32, ctypes.c_double, _P]
         L.ref_heat_problem.restype = ctypes.c_double
         L.ref_num_threads.restype = ctypes.c_int
+        L.ref_set_num_threads.argtypes = [ctypes.c_int]
+
+    def set_num_threads(self, n):
+        """OpenMP threads of alpaka3's host backend for every later call."""
+        self.lib.ref_set_num_threads(int(n))
 
     KERNELS = {"copy": 1, "mul": 2, "add": 4, "triad": 8, "dot": 16, "nstream": 32}
 

@@ -458,6 +458,13 @@ extern "C"
         return 0;
     }
 
+    // OpenMP thread count for every later call (the process may have inherited OMP_NUM_THREADS=1 from a launcher)
+    void ref_set_num_threads(int n)
+    {
+        if(n > 0)
+            omp_set_num_threads(n);
+    }
+
     int ref_num_threads()
     {
         int t = 1;

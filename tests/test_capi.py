@@ -68,3 +68,38 @@ def test_halo_mailbox_layout_and_argument_checks_without_gpu():
     assert "halo" in capi.last_error()
     assert L.a3b_heat_halo_publish(None, None, None, 10, 10, 12) == capi.ERR_INVALID
     assert L.a3b_halo_destroy(None) == capi.OK
+
+
+def test_early_start_guard_host_bookkeeping_without_gpu():
+    """The reductions' early-start guard (host only): off by default; once enabled, a call reading the output of any
+    reduction started early since the last fully ordered launch is launched fully ordered (which clears the history),
+    repeated outputs are remembered once, and a history past 64 outputs forces one ordered launch."""
+    from alpaka3_b200 import capi
+    L = capi.lib()
+    s = ctypes.c_void_p(0x5000)  # stands for a stream; the hooks never pass it to CUDA
+    x, y = 0x10000000, 0x20000000
+    o = [0x30000000 + 256 * k for k in range(80)]
+    flag = ctypes.c_int(-1)
+
+    def probe(in0, out, in1=None, nbytes=4096):
+        capi.call("a3b_debug_early_start_probe", 7, s, ctypes.c_void_p(in0), ctypes.c_void_p(in1) if in1 else None,
+                  nbytes, ctypes.c_void_p(out), ctypes.byref(flag))
+        return flag.value
+
+    assert probe(x, o[0]) == 0  # not enabled: ordered
+    capi.call("a3b_debug_early_start_enable", 7, s, 1)
+    try:
+        assert probe(x, o[0]) == 1            # A
+        assert probe(y, o[1]) == 1            # B, unrelated
+        assert probe(o[0], o[2], nbytes=256) == 0  # C reads A's output: ordered, history cleared
+        assert probe(o[0], o[3], nbytes=256) == 1  # A completed before C started
+        assert probe(x, o[4], in1=o[3] - 8, nbytes=16) == 0  # second input overlapping an early output
+        for _ in range(100):                  # one repeated output: remembered once
+            assert probe(x, o[5]) == 1
+        for k in range(6, 68):                # with o[4] and o[5]: 64 distinct outputs in the history now
+            assert probe(x, o[k]) == 1
+        assert probe(x, o[70]) == 0           # past the limit: ordered
+        assert probe(x, o[71]) == 1
+    finally:
+        capi.call("a3b_debug_early_start_enable", 7, s, 0)
+    assert probe(x, o[0]) == 0

@@ -146,6 +146,7 @@ def test_fused_reduce_one_rank_back_to_back_and_chained(cuda, port):
     algo.random_f32(x, SEED, -1.0, 1.0)
     want = port.sumsq(port.gen_f32(n, -1.0, 1.0))
     g = adist.PeerGroup()
+    algo.set_early_start(True)
     try:
         outs = [torch.empty(1, dtype=torch.float32, device=cuda) for _ in range(8)]
         for o in outs:
@@ -162,6 +163,7 @@ def test_fused_reduce_one_rank_back_to_back_and_chained(cuda, port):
             torch.cuda.synchronize()
             assert float(total.item()) == float(buf[0].item()) == vals[0]
     finally:
+        algo.set_early_start(False)
         g.close()
 
 
@@ -175,6 +177,14 @@ def test_plain_reduce_back_to_back_and_chained(cuda, port):
     x = torch.empty(n, dtype=torch.float32, device=cuda)
     algo.random_f32(x, SEED, -1.0, 1.0)
     want = port.sumsq(port.gen_f32(n, -1.0, 1.0))
+    algo.set_early_start(True)
+    try:
+        _plain_chained(algo, x, want, cuda)
+    finally:
+        algo.set_early_start(False)
+
+
+def _plain_chained(algo, x, want, cuda):
     outs = [torch.empty(1, dtype=torch.float32, device=cuda) for _ in range(8)]
     for o in outs:
         algo.transform_reduce(0.0, o, "plus", "square", x)
@@ -192,3 +202,67 @@ def test_plain_reduce_back_to_back_and_chained(cuda, port):
         algo.reduce(0.0, total, "plus", grid[:, :32])
         torch.cuda.synchronize()
         assert float(total.item()) == vals[0]
+
+
+def test_early_start_three_call_chain(cuda, port):
+    """A writes buf[0], an unrelated call B (early start) follows, then C reduces buf: C must see A's output although
+    A may still run while B starts (the guard remembers every early-started call since the last ordered launch)."""
+    from alpaka3_b200 import algo
+    from oracle.oracle import SEED
+    n = (1 << 24) + 7
+    x = torch.empty(n, dtype=torch.float32, device=cuda)
+    algo.random_f32(x, SEED, -1.0, 1.0)
+    ref = torch.empty(1, dtype=torch.float32, device=cuda)
+    algo.transform_reduce(0.0, ref, "plus", "square", x)
+    torch.cuda.synchronize()
+    want = float(ref.item())
+    buf = torch.zeros(64, dtype=torch.float32, device=cuda)
+    other = torch.empty(1, dtype=torch.float32, device=cuda)
+    total = torch.empty(1, dtype=torch.float32, device=cuda)
+    algo.set_early_start(True)
+    try:
+        for _ in range(6):
+            algo.transform_reduce(0.0, buf[0:1], "plus", "square", x)   # A
+            algo.transform_reduce(0.0, other, "plus", "square", x)      # B: input x, not A's output
+            algo.transform_reduce(0.0, total, "plus", "identity", buf)  # C: reads A's output
+            torch.cuda.synchronize()
+            assert float(total.item()) == float(buf[0].item()) == want
+            assert float(other.item()) == want
+    finally:
+        algo.set_early_start(False)
+
+
+def test_early_start_history_overflow_then_dependent(cuda):
+    """More than 64 early-started calls (the guard's history limit), then a call reading the output of one of them."""
+    from alpaka3_b200 import algo
+    n = (1 << 20) + 3
+    x = torch.rand(n, dtype=torch.float32, device=cuda) * 2 - 1
+    ref = torch.empty(1, dtype=torch.float32, device=cuda)
+    algo.transform_reduce(0.0, ref, "plus", "square", x)
+    torch.cuda.synchronize()
+    want = float(ref.item())
+    outs = torch.zeros(100, dtype=torch.float32, device=cuda)
+    total = torch.empty(1, dtype=torch.float32, device=cuda)
+    algo.set_early_start(True)
+    try:
+        for k in range(100):
+            algo.transform_reduce(0.0, outs[k:k + 1], "plus", "square", x)
+        algo.transform_reduce(0.0, total, "plus", "identity", outs)
+        torch.cuda.synchronize()
+        assert (outs.cpu() == want).all()
+        assert abs(float(total.item()) - 100 * want) <= 1e-5 * 100 * want
+    finally:
+        algo.set_early_start(False)
+
+
+def test_early_start_off_by_default_is_ordered(cuda):
+    """Without a3b_set_early_start the reductions are plain launches: a torch kernel writing the input just before
+    the call is complete before the call reads it (here trivially, but the default must stay ordered)."""
+    from alpaka3_b200 import algo
+    x = torch.empty((1 << 22) + 5, dtype=torch.float32, device=cuda)
+    out = torch.empty(1, dtype=torch.float32, device=cuda)
+    for v in (1.0, 2.0, 3.0):
+        x.fill_(v)
+        algo.transform_reduce(0.0, out, "plus", "identity", x)
+        torch.cuda.synchronize()
+        assert float(out.item()) == v * x.numel()
