@@ -92,8 +92,7 @@ namespace a3b
     {
         kScratchReduce = 0,
         kScratchScan = 1,
-        kScratchNbody = 2,
-        kScratchSlots = 3
+        kScratchSlots = 2
     };
     // With `epoch` non-null, also hands out the next call epoch of this scratch (30 bits, never 0): kernels that tag
     // their scratch words with the epoch need no clearing between calls on the stream.

@@ -305,7 +305,10 @@ void orc_heat_step(double const* cur, double* next, uint32_t n, double rX, doubl
 
 /* One step: velocity kick over all j in index order (Kernels.hpp:90-121), then the drift (Kernels.hpp:126-142).
  * Per pair: d = p_j - p_i; r2 = (dx*dx + (dy*dy + dz*dz)) + eps (the Simd<3> tree sum); r6 = r2*r2*r2;
- * inv = 1/sqrt(r6); s = m_j*inv; a += s*d. Then v += a*dt, x += v*dt. */
+ * inv = 1/sqrt(r6); s = m_j*inv; a += s*d. Then v += a*dt, x += v*dt.
+ * The i-bodies are taken 16 at a time so the compiler can vectorise across them; every body still accumulates its
+ * pairs one j after the other in index order, so each result is the same as a scalar loop over j. */
+#define ORC_NB_IB 16
 void orc_nbody_step(
     float const* m,
     float* x,
@@ -318,27 +321,42 @@ void orc_nbody_step(
     float dt,
     float eps)
 {
-#pragma omp parallel for schedule(static)
-    for(int64_t i = 0; i < (int64_t)n; ++i)
+#pragma omp parallel for schedule(dynamic, 4)
+    for(int64_t i0 = 0; i0 < (int64_t)n; i0 += ORC_NB_IB)
     {
-        float const xi = x[i], yi = y[i], zi = z[i];
-        float ax = 0.f, ay = 0.f, az = 0.f;
+        int const cnt = (int64_t)n - i0 < ORC_NB_IB ? (int)((int64_t)n - i0) : ORC_NB_IB;
+        float xi[ORC_NB_IB], yi[ORC_NB_IB], zi[ORC_NB_IB], ax[ORC_NB_IB], ay[ORC_NB_IB], az[ORC_NB_IB];
+        for(int k = 0; k < ORC_NB_IB; ++k)
+        {
+            int64_t const i = i0 + (k < cnt ? k : 0);
+            xi[k] = x[i];
+            yi[k] = y[i];
+            zi[k] = z[i];
+            ax[k] = ay[k] = az[k] = 0.f;
+        }
         for(uint64_t j = 0; j < n; ++j)
         {
-            float const dx = x[j] - xi;
-            float const dy = y[j] - yi;
-            float const dz = z[j] - zi;
-            float const r2 = (dx * dx + (dy * dy + dz * dz)) + eps;
-            float const r6 = r2 * r2 * r2;
-            float const inv = 1.0f / sqrtf(r6);
-            float const s = m[j] * inv;
-            ax += s * dx;
-            ay += s * dy;
-            az += s * dz;
+            float const xj = x[j], yj = y[j], zj = z[j], mj = m[j];
+            for(int k = 0; k < ORC_NB_IB; ++k)
+            {
+                float const dx = xj - xi[k];
+                float const dy = yj - yi[k];
+                float const dz = zj - zi[k];
+                float const r2 = (dx * dx + (dy * dy + dz * dz)) + eps;
+                float const r6 = r2 * r2 * r2;
+                float const inv = 1.0f / sqrtf(r6);
+                float const s = mj * inv;
+                ax[k] += s * dx;
+                ay[k] += s * dy;
+                az[k] += s * dz;
+            }
         }
-        vx[i] += ax * dt;
-        vy[i] += ay * dt;
-        vz[i] += az * dt;
+        for(int k = 0; k < cnt; ++k)
+        {
+            vx[i0 + k] += ax[k] * dt;
+            vy[i0 + k] += ay[k] * dt;
+            vz[i0 + k] += az[k] * dt;
+        }
     }
 #pragma omp parallel for schedule(static)
     for(int64_t i = 0; i < (int64_t)n; ++i)
@@ -349,8 +367,7 @@ void orc_nbody_step(
     }
 }
 
-/* Accelerations of the bodies listed in `idx` against all n bodies, accumulated in fp64 (a sampled checker for
- * full-size runs where the O(n^2) oracle would be too slow). */
+/* fp64 accelerations of the sampled bodies idx[0..k) (all-pairs sum in double; a size-independent check) */
 void orc_nbody_accel_sample(
     float const* m,
     float const* x,

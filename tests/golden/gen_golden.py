@@ -14,6 +14,13 @@ The fixtures are small (hashes, scalars, a few KB of arrays) and are committed; 
   sumsq.json          transformReduce(plus, x*x) over 2^20 seeded fp32 in [-1, 1) (reference fp32 value)
   heat_problem.npz    the heatEquation2D example's own problem at its defaults (64 x 64, 4000 steps, tMax 0.1: exact
                       initial field, time-dependent Dirichlet ring): final field and the example's validation error
+  nbody_262144.npz    the nBody workload itself: 262144 bodies (positions uniform in the unit cube, masses uniform in
+                      [0.5, 1), velocities 0, seeded Philox streams), eps^2 = 1e-3, dt = 1e-3, 10 kick + drift steps:
+                      final positions. The reference kernel hard-codes EPS = 4 (example/nBody/src/common.hpp:41), so
+                      these come from the oracle restatement (oracle.c), which nbody.npz pins bit-exact to the
+                      reference kernel at EPS = 4 (about a minute on 8 cores).
+
+usage: python tests/golden/gen_golden.py [fixture-name ...]   (default: all)
 """
 import hashlib
 import json
@@ -35,8 +42,26 @@ def sha(a):
     return hashlib.sha256(np.ascontiguousarray(a).tobytes()).hexdigest()
 
 
+def nbody_full(port):
+    n, steps, dt, eps = 262144, 10, 1e-3, 1e-3
+    m = port.gen_f32(n, 0.5, 1.0, seed=SEED + 1)
+    pos = [port.gen_f32(n, 0.0, 1.0, seed=SEED + s) for s in (2, 3, 4)]
+    zeros = np.zeros(n, np.float32)
+    out = port.nbody_steps(m, *pos, zeros, zeros, zeros, dt, eps, steps)
+    np.savez_compressed(os.path.join(HERE, "nbody_262144.npz"), x=out[0], y=out[1], z=out[2], n=n, steps=steps, dt=dt,
+                        eps=eps, vmax=max(float(np.max(np.abs(v))) for v in out[3:]),
+                        input_sha256=sha(np.stack([m, *pos])))
+
+
 def main():
-    ref, port = Ref(), Port()
+    port = Port()
+    only = set(sys.argv[1:])
+    if only:
+        if "nbody_262144" in only:
+            nbody_full(port)
+        print("written:", sorted(only))
+        return
+    ref = Ref()
     scan = {}
     for n in SCAN_SIZES:
         x = np.arange(n, dtype=np.int64).astype(np.int32)
@@ -81,6 +106,7 @@ def main():
               open(os.path.join(HERE, "sumsq.json"), "w"), indent=1)
     u, err = ref.heat_problem(64, 4000, 0.1)
     np.savez_compressed(os.path.join(HERE, "heat_problem.npz"), u=u, err=err, n=64, steps=4000, t_max=0.1)
+    nbody_full(port)
     print("golden fixtures written to", HERE)
 
 

@@ -102,3 +102,33 @@ def test_nbody_262144_sampled(cuda, port):
         p = (M.double() * c.double()).sum().item()
         scale = (M.double() * c.double().abs()).sum().item()
         assert abs(p) <= 1e-4 * scale
+
+
+def test_nbody_262144_ten_steps_against_golden(cuda):
+    """The nBody workload itself: 262144 bodies (unit cube, masses [0.5, 1), v = 0), eps^2 = 1e-3, dt = 1e-3, ten
+    kick + drift steps through the C ABI; final positions within 1e-4 (normwise, max |error| / max |position| per
+    component) of the oracle's trajectory (tests/golden/nbody_262144.npz; the oracle follows the reference kernel's
+    operation order, pinned bit-exact to it by nbody.npz). The configuration collapses violently (peak speed ~7200,
+    positions spread to ~65), which makes it sensitive to the order of the j sums."""
+    import os
+
+    import numpy as np
+    from alpaka3_b200 import algo
+    from conftest import GOLDEN
+    from oracle.oracle import SEED
+    g = np.load(os.path.join(GOLDEN, "nbody_262144.npz"))
+    n, steps, dt, eps = int(g["n"]), int(g["steps"]), float(g["dt"]), float(g["eps"])
+    m = torch.empty(n, dtype=torch.float32, device=cuda)
+    algo.random_f32(m, SEED + 1, 0.5, 1.0)
+    pos = [torch.empty(n, dtype=torch.float32, device=cuda) for _ in range(3)]
+    for k, t in enumerate(pos):
+        algo.random_f32(t, SEED + 2 + k, 0.0, 1.0)
+    v = [torch.zeros(n, dtype=torch.float32, device=cuda) for _ in range(3)]
+    for _ in range(steps):
+        algo.nbody_step(m, *pos, *v, dt, eps)
+    torch.cuda.synchronize()
+    for t, key in zip(pos, "xyz"):
+        want = g[key]
+        got = t.cpu().numpy()
+        rel = float(np.max(np.abs(got - want)) / np.max(np.abs(want)))
+        assert rel <= 1e-4, (key, rel)
