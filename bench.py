@@ -45,6 +45,13 @@ def host_threads():
         return os.cpu_count() or 1
 
 
+def use_all_host_threads():
+    """Before the OpenMP runtime of the CPU arms is loaded: alpaka3's host queue runs its kernels on a worker thread of
+    its own, whose OpenMP thread count comes from OMP_NUM_THREADS when the runtime starts (a later omp_set_num_threads
+    on this thread does not reach it)."""
+    os.environ["OMP_NUM_THREADS"] = str(host_threads())
+
+
 def peaks():
     try:
         with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
@@ -400,6 +407,7 @@ def _wrap(torch, ev, fn):
 def cpu_baseline(budget_s=8.0, n=1 << 28):
     """alpaka3's own transformReduce on exec::cpuOmpBlocks over a 2^28 fp32 sample (1.07 GB), repeated for about
     budget_s seconds; GB/s of input read."""
+    use_all_host_threads()
     try:
         from oracle.oracle import Port, Ref
         ref, port = Ref(), Port()
@@ -426,6 +434,7 @@ def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
+    use_all_host_threads()
     try:
         from oracle.oracle import Port, Ref
         ref, port = Ref(), Port()
