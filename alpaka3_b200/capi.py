@@ -44,6 +44,7 @@ SIGNATURES = {
     "a3b_stream_synchronize": [_P],
     "a3b_get_device_error": [_P, _P, _I],
     "a3b_set_wait_timeout_ns": [_U64],
+    "a3b_engine_scratch": [_P, ctypes.c_size_t, _P],
     "a3b_babelstream": [_P, _I, _I, _P, _P, _P, _U64, _D, _P],
     "a3b_transform": [_P, _I, _I, _P, _P, _P, _U64, _D],
     "a3b_fill": [_P, _I, _P, _U64, _P],

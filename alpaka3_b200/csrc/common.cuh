@@ -92,7 +92,8 @@ namespace a3b
     {
         kScratchReduce = 0,
         kScratchScan = 1,
-        kScratchSlots = 2
+        kScratchEngine = 2, // kernels of the header-only engines (a3b_engine_scratch)
+        kScratchSlots = 3
     };
     // With `epoch` non-null, also hands out the next call epoch of this scratch (30 bits, never 0): kernels that tag
     // their scratch words with the epoch need no clearing between calls on the stream.

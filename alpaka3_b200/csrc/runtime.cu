@@ -141,6 +141,12 @@ extern "C"
         return tlsError.c_str();
     }
 
+    int a3b_engine_scratch(a3b_stream_t stream, size_t bytes, void** ptr)
+    {
+        A3B_REQUIRE(ptr, "ptr is null");
+        return streamScratch(static_cast<cudaStream_t>(stream), kScratchEngine, bytes > 0 ? bytes : 1, ptr);
+    }
+
     int a3b_device_count(int* count)
     {
         A3B_REQUIRE(count, "count is null");

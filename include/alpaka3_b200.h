@@ -114,6 +114,11 @@ A3B_API int a3b_free_async(void* ptr, a3b_stream_t stream);
 A3B_API int a3b_memcpy_async(void* dst, void const* src, size_t bytes, a3b_stream_t stream);
 /* onHost::wait(queue) (include/alpaka/onHost/interface.hpp:142) */
 A3B_API int a3b_stream_synchronize(a3b_stream_t stream);
+/* Device scratch for the kernels that the header-only engines (include/alpaka3_b200/simd_engine.cuh) instantiate in
+ * the caller's translation unit: at least `bytes`, cached per (device, stream), zero-filled when first allocated or
+ * grown. Work ordered on `stream` may use it; the engines leave it as they found it (their tickets are reset by the
+ * kernel that drew the last number). No counterpart in alpaka3, whose reductions pre-fill the output instead. */
+A3B_API int a3b_engine_scratch(a3b_stream_t stream, size_t bytes, void** ptr);
 /* Reads (and with clear != 0 resets) the device-side error word of the current device: bit 0 = a bounded wait timed
  * out (A3B_ERR_TIMEOUT). Synchronises `stream`. */
 A3B_API int a3b_get_device_error(a3b_stream_t stream, uint32_t* error_bits, int clear);

@@ -4,25 +4,33 @@
  *   alpaka::onHost::transformReduce   (alpaka3: include/alpaka/onHost/algo/transformReduce.hpp:59-114)
  *   alpaka::onHost::reduce            (include/alpaka/onHost/algo/reduce.hpp:28-79)
  *   alpaka::onHost::exclusiveScan / inclusiveScan / *InPlace   (include/alpaka/onHost/algo/scan.hpp:45-218)
- *   alpaka::onHost::transform         (include/alpaka/onHost/algo/transform.hpp:50-88; nvcc translation units only)
+ *   alpaka::onHost::transform         (include/alpaka/onHost/algo/transform.hpp:50-88)
+ *   alpaka::onHost::concurrent        (include/alpaka/onHost/algo/concurrent.hpp:44-82)
  *   alpaka::onHost::iota              (include/alpaka/onHost/algo/iota.hpp:29-85)
  *   alpaka::onHost::fill              (include/alpaka/onHost/Queue.hpp:346)
  * for queues of CUDA devices (Queue<Device<api::Cuda, K>, Q>). Partial ordering picks them over alpaka3's generic
- * templates because their queue parameter is more specialised. At run time a call goes to the C ABI when
- *   - the element type is int32/uint32/int64/uint64/float/double,
- *   - the data are device buffers (IMdSpan) laid out densely, or as rows with one constant pitch,
- *   - the reduce functor is std::plus or (probed on the host) computes +, min or max, and the transform functor is
- *     std::identity or computes x, x*x or a*b (probed with scalars, or with Simd<T, 1> for functors such as
- *     BabelStream's DotMultiplication that take SIMD packs);
- * transform with any functor that takes alpaka::Simd packs (or a ScalarFunc taking scalars) and no accelerator, on
- * device buffers of equal extents laid out densely or as pitched rows, runs the B200 element-wise engine of
- * elementwise.cuh, compiled here by nvcc with the caller's functor;
- * fill of a dense buffer of those element types, and iota into one dense integer buffer of the iota's own type
- * (alpaka3's floating-point iota rounds per SIMD pack, so it stays on alpaka3's kernel), go to a3b_fill / a3b_iota;
- * every other call is forwarded unchanged to alpaka3's own implementation (onHost::internal::transformReduce /
- * internal::scan), so the caller's results never depend on the routing. Backend errors throw std::runtime_error, as
- * alpaka3's ALPAKA_UNIFORM_CUDA_HIP_RT_CHECK does (include/alpaka/core/UniformCudaHip.hpp:42). Blocking queues wait
- * for the call to finish.
+ * templates because their queue parameter is more specialised. A call runs on one of three paths:
+ *
+ *   1. the library's tuned kernels through the C ABI, when the functors are known by their TYPE: std::plus (or a
+ *      ScalarFunc around a type declared below) as the reduce functor, std::identity (one input) or std::multiplies
+ *      (two inputs) as the transform; int32/uint32/int64/uint64/float/double device buffers laid out densely or as
+ *      rows with one constant pitch. A caller declares its own functor types with the traits
+ *      alpaka3_b200::ReduceKind<F> / TransformKind<F> (e.g. BabelStream's DotMultiplication as A3B_XFORM_PRODUCT).
+ *      Scans with + of those types, fill of dense buffers and integer iota into one dense buffer also go here.
+ *      Classifying unknown functor types by evaluating them on a few values is available behind
+ *      ALPAKA3_B200_PROBE_FUNCTORS (off by default: a functor that agrees with x*x on small positive values but not
+ *      on negative ones would be misrouted);
+ *   2. in translation units compiled by nvcc, every other transformReduce / reduce / transform / concurrent call runs
+ *      on the B200 engines compiled here with the caller's functors: include/alpaka3_b200/elementwise.cuh for
+ *      transforms of SIMD or scalar functors over plain device buffers, include/alpaka3_b200/simd_engine.cuh for the
+ *      rest (StencilFunc and ScalarFunc functors, functors that take an accelerator, generator sources such as
+ *      LinearizedIdxGenerator, up-casting outputs, any reduce functor); they call the functors exactly as alpaka3
+ *      does (SimdPtr / Simd packs, optional accelerator first argument);
+ *   3. anything else (host translation units without nvcc, unsupported data sources) is forwarded unchanged to
+ *      alpaka3's own implementation (onHost::internal::*).
+ * alpaka3_b200::routingStats() counts the calls per path. Backend errors throw std::runtime_error, as alpaka3's
+ * ALPAKA_UNIFORM_CUDA_HIP_RT_CHECK does (include/alpaka/core/UniformCudaHip.hpp:42). Blocking queues wait for the
+ * call to finish.
  */
 #pragma once
 
@@ -31,6 +39,7 @@
 #include "../alpaka3_b200.h"
 #if defined(__CUDACC__)
 #    include "elementwise.cuh"
+#    include "simd_engine.cuh"
 #endif
 
 #include <atomic>
@@ -44,11 +53,62 @@
 
 namespace alpaka3_b200
 {
-    //! How many calls this process routed to the C ABI / forwarded to alpaka3's own implementation.
+    //! How many calls this process sent to the library (C ABI or a B200 engine compiled here: `routed`, of which
+    //! `engine` ran on an engine) / forwarded to alpaka3's own implementation.
     struct RoutingStats
     {
         std::atomic<std::uint64_t> routed{0};
+        std::atomic<std::uint64_t> engine{0};
         std::atomic<std::uint64_t> forwarded{0};
+    };
+
+    /** What a reduce functor type computes, for the C ABI path: A3B_REDUCE_PLUS / _MIN / _MAX, or -1 (unknown: the
+     * call runs on the engine with the functor itself). Specialise for your own functor types. */
+    template<typename F>
+    struct ReduceKind : std::integral_constant<int, -1>
+    {
+    };
+
+    template<>
+    struct ReduceKind<std::plus<>> : std::integral_constant<int, A3B_REDUCE_PLUS>
+    {
+    };
+
+    template<typename T>
+    struct ReduceKind<std::plus<T>> : std::integral_constant<int, A3B_REDUCE_PLUS>
+    {
+    };
+
+    template<typename F>
+    struct ReduceKind<alpaka::ScalarFunc<F>> : ReduceKind<F>
+    {
+    };
+
+    /** What a transform functor type computes: A3B_XFORM_IDENTITY (one input), A3B_XFORM_SQUARE (one input, x*x),
+     * A3B_XFORM_PRODUCT (two inputs, a*b), or -1. Specialise for your own functor types. */
+    template<typename F>
+    struct TransformKind : std::integral_constant<int, -1>
+    {
+    };
+
+    template<>
+    struct TransformKind<std::identity> : std::integral_constant<int, A3B_XFORM_IDENTITY>
+    {
+    };
+
+    template<>
+    struct TransformKind<std::multiplies<>> : std::integral_constant<int, A3B_XFORM_PRODUCT>
+    {
+    };
+
+    template<typename T>
+    struct TransformKind<std::multiplies<T>> : std::integral_constant<int, A3B_XFORM_PRODUCT>
+    {
+    };
+
+    template<typename F>
+    struct TransformKind<alpaka::ScalarFunc<F>> : TransformKind<F>
+    {
     };
 
     inline RoutingStats& routingStats()
@@ -111,11 +171,12 @@ namespace alpaka3_b200
         }
 
         template<typename T, typename F>
-        int reduceOpOf(F const& f)
+        int reduceOpOf([[maybe_unused]] F const& f)
         {
             using D = std::decay_t<F>;
-            if constexpr(std::is_same_v<D, std::plus<>> || std::is_same_v<D, std::plus<T>>)
-                return A3B_REDUCE_PLUS;
+            if constexpr(ReduceKind<D>::value >= 0)
+                return ReduceKind<D>::value;
+#if defined(ALPAKA3_B200_PROBE_FUNCTORS)
             else
             {
                 auto const a = probe<T>(f, T(3), T(5)), b = probe<T>(f, T(5), T(3)), c = probe<T>(f, T(7), T(2));
@@ -129,27 +190,30 @@ namespace alpaka3_b200
                     return A3B_REDUCE_MAX;
                 return -1;
             }
+#else
+            else
+                return -1;
+#endif
         }
 
         template<typename T, int NIN, typename F>
-        int transformOpOf(F const& f)
+        int transformOpOf([[maybe_unused]] F const& f)
         {
             using D = std::decay_t<F>;
-            if constexpr(NIN == 1)
+            constexpr int kind = TransformKind<D>::value;
+            if constexpr(kind >= 0)
+                return (kind == A3B_XFORM_PRODUCT) == (NIN == 2) ? kind : -1;
+#if defined(ALPAKA3_B200_PROBE_FUNCTORS)
+            else if constexpr(NIN == 1)
             {
-                if constexpr(std::is_same_v<D, std::identity>)
-                    return A3B_XFORM_IDENTITY;
-                else
-                {
-                    auto const a = probe<T>(f, T(3)), b = probe<T>(f, T(5));
-                    if(!a || !b)
-                        return -1;
-                    if(*a == T(3) && *b == T(5))
-                        return A3B_XFORM_IDENTITY;
-                    if(*a == T(9) && *b == T(25))
-                        return A3B_XFORM_SQUARE;
+                auto const a = probe<T>(f, T(3)), b = probe<T>(f, T(5));
+                if(!a || !b)
                     return -1;
-                }
+                if(*a == T(3) && *b == T(5))
+                    return A3B_XFORM_IDENTITY;
+                if(*a == T(9) && *b == T(25))
+                    return A3B_XFORM_SQUARE;
+                return -1;
             }
             else if constexpr(NIN == 2)
             {
@@ -158,6 +222,7 @@ namespace alpaka3_b200
                     return A3B_XFORM_PRODUCT;
                 return -1;
             }
+#endif
             else
                 return -1;
         }
@@ -490,6 +555,120 @@ namespace alpaka3_b200
             else
                 return exec;
         }
+
+#if defined(__CUDACC__)
+        template<typename A, typename... R>
+        A const& firstOf(A const& a, R const&...)
+        {
+            return a;
+        }
+
+        inline void engineCheck(cudaError_t e, char const* what)
+        {
+            if(e != cudaSuccess)
+                throw std::runtime_error(std::string(what) + ": " + cudaGetErrorString(e));
+        }
+
+        template<typename Q>
+        void engineDone(Q const& queue)
+        {
+            finish(queue);
+            ++routingStats().routed;
+            ++routingStats().engine;
+        }
+
+        //! transformReduce / reduce with any functors on the B200 engine (simd_engine.cuh): fold over the lanes of
+        //! the transformed packs, one launch, out[0] written by the last block.
+        template<typename TApi, typename TDeviceKind, typename T, typename Q>
+        void engineTransformReduce(
+            Q const& queue,
+            auto exec,
+            T const& neutral,
+            auto& out,
+            auto const& reduceFn,
+            auto const& transformFn,
+            auto const&... in)
+        {
+            using TExec = std::decay_t<decltype(resolveExec(queue, exec))>;
+            auto* const outPtr = const_cast<T*>(static_cast<T const*>(alpaka::onHost::data(out)));
+            engineCheck(
+                simd::reduce<TApi, TDeviceKind, TExec>(
+                    static_cast<cudaStream_t>(streamOf(queue)),
+                    alpaka::onHost::getExtents(firstOf(in...)),
+                    neutral,
+                    reduceFn,
+                    simd::ReduceTransform<std::decay_t<decltype(transformFn)>>{transformFn},
+                    outPtr,
+                    alpaka::onHost::makeAccessibleOnAcc(in)...),
+                "alpaka3_b200 transformReduce engine");
+            engineDone(queue);
+        }
+
+        //! transform with any functor on the B200 engine: out = fn(in...) over out's extents.
+        template<typename TApi, typename TDeviceKind, typename Q>
+        void engineTransform(Q const& queue, auto exec, auto& out, auto const& fn, auto const&... in)
+        {
+            using TExec = std::decay_t<decltype(resolveExec(queue, exec))>;
+            engineCheck(
+                simd::each<TApi, TDeviceKind, TExec>(
+                    static_cast<cudaStream_t>(streamOf(queue)),
+                    alpaka::onHost::getExtents(out),
+                    simd::TransformBody<std::decay_t<decltype(fn)>>{fn},
+                    alpaka::onHost::makeAccessibleOnAcc(out),
+                    alpaka::onHost::makeAccessibleOnAcc(in)...),
+                "alpaka3_b200 transform engine");
+            engineDone(queue);
+        }
+
+        //! iota into any number of outputs on the B200 engine
+        template<typename TApi, typename TDeviceKind, typename T, typename Q>
+        void engineIota(Q const& queue, auto exec, T const& init, auto&& out0, auto&&... outs)
+        {
+            using TExec = std::decay_t<decltype(resolveExec(queue, exec))>;
+            auto const ext = alpaka::onHost::getExtents(out0);
+            using Ext = typename std::decay_t<decltype(ext)>::UniVec;
+            engineCheck(
+                simd::each<TApi, TDeviceKind, TExec>(
+                    static_cast<cudaStream_t>(streamOf(queue)),
+                    ext,
+                    simd::IotaBody<T, Ext>{Ext{ext}, init},
+                    alpaka::onHost::makeAccessibleOnAcc(out0),
+                    alpaka::onHost::makeAccessibleOnAcc(outs)...),
+                "alpaka3_b200 iota engine");
+            engineDone(queue);
+        }
+
+        //! fill of any device buffer layout on the B200 engine
+        template<typename TApi, typename TDeviceKind, typename T, typename Q>
+        void engineFill(Q const& queue, auto&& dest, T const& value)
+        {
+            using TExec = std::decay_t<decltype(alpaka::onHost::defaultExecutor(queue.getDevice()))>;
+            engineCheck(
+                simd::each<TApi, TDeviceKind, TExec>(
+                    static_cast<cudaStream_t>(streamOf(queue)),
+                    alpaka::onHost::getExtents(dest),
+                    simd::FillBody<T>{value},
+                    alpaka::onHost::makeAccessibleOnAcc(dest)),
+                "alpaka3_b200 fill engine");
+            engineDone(queue);
+        }
+
+        //! concurrent on the B200 engine: fn(acc?, SimdPtr...) over `extents`.
+        template<typename TApi, typename TDeviceKind, typename Q>
+        void engineConcurrent(Q const& queue, auto exec, auto const& extents, auto const& fn, auto&&... inOut)
+        {
+            using TExec = std::decay_t<decltype(resolveExec(queue, exec))>;
+            alpaka::Vec const ext = extents;
+            engineCheck(
+                simd::each<TApi, TDeviceKind, TExec>(
+                    static_cast<cudaStream_t>(streamOf(queue)),
+                    ext,
+                    simd::ConcurrentBody<std::decay_t<decltype(fn)>>{fn},
+                    alpaka::onHost::makeAccessibleOnAcc(inOut)...),
+                "alpaka3_b200 concurrent engine");
+            engineDone(queue);
+        }
+#endif
     } // namespace detail
 } // namespace alpaka3_b200
 
@@ -509,6 +688,20 @@ namespace alpaka::onHost
     {
         if(alpaka3_b200::detail::tryTransformReduce<DataType>(queue, neutralElement, out, binaryReduceFn, transformFn, in...))
             return;
+#if defined(__CUDACC__)
+        if constexpr(std::is_trivially_copyable_v<DataType>)
+        {
+            alpaka3_b200::detail::engineTransformReduce<api::Cuda, T_DeviceKind>(
+                queue,
+                exec,
+                neutralElement,
+                out,
+                binaryReduceFn,
+                transformFn,
+                in...);
+            return;
+        }
+#endif
         ++alpaka3_b200::routingStats().forwarded;
         internal::transformReduce(
             queue,
@@ -552,6 +745,20 @@ namespace alpaka::onHost
     {
         if(alpaka3_b200::detail::tryTransformReduce<DataType>(queue, neutralElement, out, binaryReduceFn, std::identity{}, in))
             return;
+#if defined(__CUDACC__)
+        if constexpr(std::is_trivially_copyable_v<DataType>)
+        {
+            alpaka3_b200::detail::engineTransformReduce<api::Cuda, T_DeviceKind>(
+                queue,
+                exec,
+                neutralElement,
+                out,
+                binaryReduceFn,
+                std::identity{},
+                in);
+            return;
+        }
+#endif
         ++alpaka3_b200::routingStats().forwarded;
         internal::transformReduce(
             queue,
@@ -663,6 +870,10 @@ namespace alpaka::onHost
     {
         if(alpaka3_b200::detail::tryIota(queue, initValue, out0, outOther...))
             return;
+#if defined(__CUDACC__)
+        alpaka3_b200::detail::engineIota<api::Cuda, T_DeviceKind>(queue, exec, initValue, out0, outOther...);
+        return;
+#endif
         ++alpaka3_b200::routingStats().forwarded;
         internal::iota<T_DataType>(
             queue,
@@ -702,6 +913,10 @@ namespace alpaka::onHost
     {
         if(alpaka3_b200::detail::tryFill(queue, dest, elementValue))
             return;
+#if defined(__CUDACC__)
+        alpaka3_b200::detail::engineFill<api::Cuda, T_DeviceKind>(queue, dest, elementValue);
+        return;
+#endif
         ++alpaka3_b200::routingStats().forwarded;
         fill(queue, ALPAKA_FORWARD(dest), elementValue, internal::getExtents(dest));
     }
@@ -718,6 +933,8 @@ namespace alpaka::onHost
 #if defined(__CUDACC__)
         if(alpaka3_b200::detail::tryTransform(queue, out, fn, in...))
             return;
+        alpaka3_b200::detail::engineTransform<api::Cuda, T_DeviceKind>(queue, exec, out, fn, in...);
+        return;
 #endif
         ++alpaka3_b200::routingStats().forwarded;
         internal::transform(
@@ -741,5 +958,42 @@ namespace alpaka::onHost
             ALPAKA_FORWARD(out),
             ALPAKA_FORWARD(fn),
             ALPAKA_FORWARD(in)...);
+    }
+
+    // ----------------------------------------------------------------------------------------------- concurrent
+    template<typename T_DataType, alpaka::concepts::DeviceKind T_DeviceKind, alpaka::concepts::QueueKind T_QueueKind>
+    inline void concurrent(
+        Queue<Device<api::Cuda, T_DeviceKind>, T_QueueKind> const& queue,
+        alpaka::concepts::Executor auto const exec,
+        alpaka::concepts::VectorOrScalar auto const& extents,
+        auto&& fn,
+        alpaka::concepts::IDataSource auto&&... inOut)
+    {
+#if defined(__CUDACC__)
+        alpaka3_b200::detail::engineConcurrent<api::Cuda, T_DeviceKind>(queue, exec, extents, fn, inOut...);
+#else
+        ++alpaka3_b200::routingStats().forwarded;
+        internal::concurrent<T_DataType>(
+            queue,
+            alpaka3_b200::detail::resolveExec(queue, exec),
+            extents,
+            ALPAKA_FORWARD(fn),
+            ALPAKA_FORWARD(inOut)...);
+#endif
+    }
+
+    template<typename T_DataType, alpaka::concepts::DeviceKind T_DeviceKind, alpaka::concepts::QueueKind T_QueueKind>
+    inline void concurrent(
+        Queue<Device<api::Cuda, T_DeviceKind>, T_QueueKind> const& queue,
+        alpaka::concepts::VectorOrScalar auto const& extents,
+        auto&& fn,
+        alpaka::concepts::IDataSource auto&&... inOut)
+    {
+        concurrent<T_DataType>(
+            queue,
+            defaultExecutor(queue.getDevice()),
+            extents,
+            ALPAKA_FORWARD(fn),
+            ALPAKA_FORWARD(inOut)...);
     }
 } // namespace alpaka::onHost

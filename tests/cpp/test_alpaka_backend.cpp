@@ -1,14 +1,19 @@
 /* alpaka3's own algorithm tests, re-expressed without Catch2, run through alpaka3's public onHost API on a CUDA queue
- * with the alpaka3_b200 binding included: the covered calls go to libalpaka3_b200.so, the rest to alpaka3's own CUDA
- * backend. Mirrors test/unit/algorithm/scan.cpp:74-197 (int iota, 4 sizes, exclusive/inclusive x out-of-place /
- * in-place x with/without buffer, std::exclusive_scan / std::inclusive_scan as ground truth) and
- * test/unit/algorithm/reduce.cpp:135-232 (int iota over N-D extents, plus / min / max, plus the generator source),
- * plus BabelStream's dot (benchmark/babelstream/src/babelStreamMainTest.cpp:135-141, 337-345), and
- * test/unit/algorithm/transform.cpp:147-180 (int inputs over the same N-D extents with std::minus, std::plus, a
- * StencilFunc, ScalarFunc with and without an accelerator argument, and an up-casting functor), plus an in-place
- * transform of a large 1-D float array with a ragged end, test/unit/algorithm/iota.cpp:13-118 (size_t iota over the
- * same extents, into one buffer and into two) and element-wise fill.
- * Prints one line "PASS routed=<n> forwarded=<m>" and exits 0, or lists the failures and exits 1. */
+ * with the alpaka3_b200 binding included: every call goes to libalpaka3_b200.so (C ABI) or to a B200 engine compiled
+ * here with the test's functors; none is forwarded to alpaka3's own CUDA backend. Mirrors
+ *   test/unit/algorithm/scan.cpp:74-197 (int iota, 4 sizes, exclusive/inclusive x out-of-place / in-place x
+ *     with/without buffer, std::exclusive_scan / std::inclusive_scan as ground truth),
+ *   test/unit/algorithm/reduce.cpp:135-232 (int iota over N-D extents, plus / ScalarFunc min / max, and the
+ *     LinearizedIdxGenerator source),
+ *   test/unit/algorithm/transformReduce.cpp:173-260 (six reduce / transform pairs over the same extents: std::plus,
+ *     StencilFunc with and without an accelerator, an up-casting transform, a ScalarFunc lambda, a ScalarFunc min),
+ *   test/unit/algorithm/transform.cpp:147-180 (std::minus, std::plus, StencilFunc, ScalarFunc with and without an
+ *     accelerator argument, up-casting functors) and :399-405 (the SimdPtr cross stencil over 1-D..4-D extents),
+ *   test/unit/algorithm/concurrent.cpp (StencilAddWithAcc, StencilAddMin over the same extents),
+ *   test/unit/algorithm/iota.cpp:13-118 and element-wise fill,
+ * plus BabelStream's dot (benchmark/babelstream/src/babelStreamMainTest.cpp:135-141, 337-345), a large in-place
+ * transform with a ragged end, and a ScalarFunc x * |x| on negative inputs (a functor that agrees with x * x on
+ * positive values). Prints "PASS routed=<n> engine=<e> forwarded=<m>" and exits 0, or lists the failures and exits 1. */
 #include <alpaka3_b200/alpaka_backend.hpp>
 
 #include <cstdio>
@@ -65,11 +70,19 @@ namespace
         }
     };
 
-    struct Cube // not recognised: must be forwarded to alpaka3's own implementation
+    struct Cube // no known type: runs on the engine with the functor itself
     {
         constexpr auto operator()(auto const& x) const
         {
             return x * x * x;
+        }
+    };
+
+    struct SignedSquare
+    {
+        ALPAKA_FN_ACC float operator()(float x) const
+        {
+            return x * (x < 0.f ? -x : x);
         }
     };
 
@@ -219,11 +232,11 @@ namespace
         auto minPlusOne = [](int x, int y) { return std::min(x + 1, y); };
         transformOne<int>(dev, queue, exec, extents, std::minus{}, minus, true, "transform minus");
         transformOne<int>(dev, queue, exec, extents, std::plus{}, plus, true, "transform plus");
-        transformOne<int>(dev, queue, exec, extents, StencilFunc{StencilAdd{}}, plus, false, "transform stencil");
+        transformOne<int>(dev, queue, exec, extents, StencilFunc{StencilAdd{}}, plus, true, "transform stencil");
         transformOne<int>(dev, queue, exec, extents, ScalarFunc{ScalarMinPlusOne{}}, minPlusOne, true, "transform scalar");
-        transformOne<int>(dev, queue, exec, extents, ScalarFunc{ScalarOpWithAcc{}}, minPlusOne, false, "transform scalar acc");
+        transformOne<int>(dev, queue, exec, extents, ScalarFunc{ScalarOpWithAcc{}}, minPlusOne, true, "transform scalar acc");
         transformOne<std::size_t>(dev, queue, exec, extents, AddUpCast{}, plus, true, "transform up-cast");
-        transformOne<std::size_t>(dev, queue, exec, extents, AddUpCastWithAcc{}, plus, false, "transform up-cast acc");
+        transformOne<std::size_t>(dev, queue, exec, extents, AddUpCastWithAcc{}, plus, true, "transform up-cast acc");
     }
 
     struct TwiceAndOne
@@ -343,7 +356,7 @@ namespace
             T const want = hostReduce<T>(op, n, op == 0 ? 0 : (op == 1 ? std::numeric_limits<T>::max() : std::numeric_limits<T>::min()));
             expect(*outHost.data() == want, "reduce", *outHost.data(), want);
         }
-        // generator source (not device memory): forwarded to alpaka3's own implementation
+        // generator source (not device memory): the engine reads it through SimdPtr like alpaka3 does
         auto generator = LinearizedIdxGenerator{extents};
         onHost::reduce(queue, exec, T{0}, out, std::plus{}, generator);
         onHost::memcpy(queue, outHost, out);
@@ -366,12 +379,227 @@ namespace
         onHost::wait(queue);
         double const want = static_cast<double>(n) * 0.1 * 0.2;
         expect(std::abs(*outHost.data() - want) <= 1e-12 * want, "dot", static_cast<long long>(*outHost.data()), static_cast<long long>(want));
-        // a transform the binding does not recognise: alpaka3's own kernel computes it
+        // a transform of no known type: the engine calls it with SIMD packs
         onHost::transformReduce(queue, exec, 0.0, out, std::plus{}, Cube{}, a);
         onHost::memcpy(queue, outHost, out);
         onHost::wait(queue);
         double const want2 = static_cast<double>(n) * (0.1 * 0.1 * 0.1);
-        expect(std::abs(*outHost.data() - want2) <= 1e-9 * want2, "transformReduce forwarded", 0, 0);
+        expect(std::abs(*outHost.data() - want2) <= 1e-9 * want2, "transformReduce cube", 0, 0);
+        // x * |x| agrees with x * x on small positive values (value probing would take it for a square) but not on
+        // negative ones: sum over x_i = -(i % 7) * 0.5 must be -sum x_i^2
+        std::size_t const m = 100003;
+        auto neg = onHost::alloc<float>(dev, Vec{m});
+        auto hneg = onHost::allocHostLike(neg);
+        double wantNeg = 0.0;
+        for(std::size_t i = 0; i < m; ++i)
+        {
+            float const x = -static_cast<float>(i % 7u) * 0.5f;
+            hneg.data()[i] = x;
+            wantNeg -= static_cast<double>(x) * x;
+        }
+        onHost::memcpy(queue, neg, hneg);
+        auto fout = onHost::alloc<float>(dev, Vec{std::size_t{1}});
+        auto fhost = onHost::allocHostLike(fout);
+        onHost::transformReduce(queue, exec, 0.f, fout, std::plus{}, ScalarFunc{SignedSquare{}}, neg);
+        onHost::memcpy(queue, fhost, fout);
+        onHost::wait(queue);
+        expect(std::abs(*fhost.data() - wantNeg) <= 1e-5 * std::abs(wantNeg), "x*|x| on negative inputs",
+               static_cast<long long>(*fhost.data()), static_cast<long long>(wantNeg));
+    }
+
+    // functors of test/unit/algorithm/transformReduce.cpp:20-82
+    struct StencilAddWithAcc
+    {
+        constexpr auto operator()(
+            onAcc::concepts::Acc auto const&,
+            concepts::SimdPtr auto const& a,
+            concepts::SimdPtr auto const& b) const
+        {
+            return a.load() + b.load();
+        }
+    };
+
+    struct MinPlusOne
+    {
+        ALPAKA_FN_ACC int operator()(int const& a, int const& b) const
+        {
+            auto lhs = a + 1;
+            return math::min(lhs, b);
+        }
+    };
+
+    //! transformReduce(neutral, out, reduceFn, transformFn, iota, iota) against a host fold
+    template<typename TOut>
+    void transformReduceOne(
+        auto& dev,
+        auto& queue,
+        auto exec,
+        auto extents,
+        TOut neutral,
+        auto reduceFn,
+        auto transformFn,
+        auto reduceRef,
+        auto transformRef,
+        char const* what)
+    {
+        using T = int;
+        auto in0 = onHost::alloc<T>(dev, extents);
+        auto in1 = onHost::allocLike(dev, in0);
+        auto host = onHost::allocHostLike(in0);
+        T c = 0;
+        for(auto& v : host)
+            v = c++;
+        onHost::memcpy(queue, in0, host);
+        onHost::memcpy(queue, in1, host);
+        auto out = onHost::alloc<TOut>(dev, extents.fill(1));
+        auto outHost = onHost::allocHostLike(out);
+        onHost::transformReduce(queue, exec, neutral, out, reduceFn, transformFn, in0, in1);
+        onHost::memcpy(queue, outHost, out);
+        onHost::wait(queue);
+        TOut want = neutral;
+        std::size_t const n = static_cast<std::size_t>(extents.product());
+        for(std::size_t i = 0; i < n; ++i)
+            want = reduceRef(want, transformRef(static_cast<T>(i), static_cast<T>(i)));
+        expect(*outHost.data() == want, what, static_cast<long long>(*outHost.data()), static_cast<long long>(want));
+    }
+
+    void transformReducePins(auto& dev, auto& queue, auto exec, auto extents)
+    {
+        // int + wraps as two's complement on the device; the host fold does the same in unsigned arithmetic
+        auto wrapPlus = [](int a, int b) { return static_cast<int>(static_cast<unsigned>(a) + static_cast<unsigned>(b)); };
+        auto minPlusOne = [](int a, int b) { return std::min(a + 1, b); };
+        auto upCast = [](int a, int b) { return static_cast<std::size_t>(a + b); };
+        auto minRef = [](int a, int b) { return std::min(a, b); };
+        transformReduceOne<int>(dev, queue, exec, extents, 0, std::plus{}, std::plus{}, wrapPlus, wrapPlus,
+                                "transformReduce plus(plus)");
+        transformReduceOne<int>(dev, queue, exec, extents, 0, std::plus{}, StencilFunc{StencilAdd{}}, wrapPlus,
+                                wrapPlus, "transformReduce plus(stencil)");
+        transformReduceOne<int>(dev, queue, exec, extents, 0, std::plus{}, StencilFunc{StencilAddWithAcc{}},
+                                wrapPlus, wrapPlus, "transformReduce plus(stencil acc)");
+        transformReduceOne<std::size_t>(dev, queue, exec, extents, std::size_t{0}, std::plus{}, AddUpCastWithAcc{},
+                                        std::plus<std::size_t>{}, upCast, "transformReduce plus(up-cast acc)");
+        transformReduceOne<int>(dev, queue, exec, extents, 0, std::plus{}, ScalarFunc{MinPlusOne{}}, wrapPlus,
+                                minPlusOne, "transformReduce plus(scalar)");
+        transformReduceOne<int>(dev, queue, exec, extents, std::numeric_limits<int>::max(), ScalarFunc{MinValue{}},
+                                std::plus{}, minRef, wrapPlus, "transformReduce min(plus)");
+    }
+
+    // functors of test/unit/algorithm/concurrent.cpp
+    struct ConcurrentAddWithAcc
+    {
+        constexpr void operator()(
+            onAcc::concepts::Acc auto const&,
+            concepts::SimdPtr auto a,
+            concepts::SimdPtr auto const& b) const
+        {
+            a = a.load() + b.load();
+        }
+    };
+
+    struct ConcurrentAddMin
+    {
+        constexpr void operator()(concepts::SimdPtr auto a, concepts::SimdPtr auto const& b) const
+        {
+            constexpr uint32_t simdWidth = a.width();
+            alpaka::concepts::Simd auto aSimd = a.load();
+            alpaka::concepts::Simd auto bSimd = b.load();
+            for(uint32_t idx = 0u; idx < simdWidth; ++idx)
+                aSimd[idx] += math::min(+aSimd[idx], +bSimd[idx]);
+            a = aSimd;
+        }
+    };
+
+    //! concurrent<int>(extents, fn, a, b) with a = b = iota; a must become want(i, i)
+    void concurrentOne(auto& dev, auto& queue, auto exec, auto extents, auto fn, auto want, char const* what)
+    {
+        using T = int;
+        auto a = onHost::alloc<T>(dev, extents);
+        auto b = onHost::allocLike(dev, a);
+        auto host = onHost::allocHostLike(a);
+        T c = 0;
+        for(auto& v : host)
+            v = c++;
+        onHost::memcpy(queue, a, host);
+        onHost::memcpy(queue, b, host);
+        onHost::concurrent<T>(queue, exec, extents, fn, a, b);
+        auto back = onHost::allocHostLike(a);
+        onHost::memcpy(queue, back, a);
+        onHost::wait(queue);
+        T i = 0;
+        int bad = 0;
+        for(auto const& v : back)
+        {
+            if(v != want(i, i) && bad++ < 3)
+                expect(false, what, v, want(i, i));
+            ++i;
+        }
+    }
+
+    void concurrentPins(auto& dev, auto& queue, auto exec, auto extents)
+    {
+        concurrentOne(dev, queue, exec, extents, ConcurrentAddWithAcc{}, [](int x, int y) { return x + y; },
+                      "concurrent add acc");
+        concurrentOne(dev, queue, exec, extents, ConcurrentAddMin{}, [](int x, int y) { return x + std::min(x, y); },
+                      "concurrent add min");
+    }
+
+    // test/unit/algorithm/transform.cpp: the cross stencil over the inner volume of a halo-padded buffer
+    struct CrossStencil
+    {
+        constexpr auto operator()(concepts::SimdPtr auto const& in) const
+        {
+            using VecIdxType = typename ALPAKA_TYPEOF(in)::IdxType;
+            concepts::Simd auto result = in.load();
+            using SimdType = ALPAKA_TYPEOF(result);
+            result += SimdType::fill(42);
+            for(uint32_t d = 0u; d < VecIdxType::dim(); ++d)
+            {
+                concepts::Vector auto negative = VecIdxType::fill(0);
+                concepts::Vector auto positive = VecIdxType::fill(0);
+                negative[d] = -1;
+                positive[d] = 1;
+                result += in[negative].load() * 3;
+                result += in[positive].load() * 5;
+            }
+            return result;
+        }
+    };
+
+    void crossStencilOne(auto& dev, auto& queue, auto exec, auto extentMd)
+    {
+        using T = int32_t;
+        using Extent = std::decay_t<decltype(extentMd)>;
+        auto const halo = Extent::fill(1);
+        auto const inner = extentMd - Extent::fill(2);
+        auto in = onHost::alloc<T>(dev, extentMd);
+        auto out = onHost::alloc<T>(dev, inner);
+        auto hin = onHost::allocHostLike(in);
+        auto hout = onHost::allocHostLike(out);
+        meta::ndLoopIncIdx(extentMd, [&](auto idx) { hin[idx] = alpaka::linearize(Extent::fill(1000), idx); });
+        onHost::memcpy(queue, in, hin);
+        auto shifted = in.getView().getSubView(halo, inner);
+        onHost::transform(queue, exec, out, StencilFunc{CrossStencil{}}, shifted);
+        onHost::memcpy(queue, hout, out);
+        onHost::wait(queue);
+        int bad = 0;
+        meta::ndLoopIncIdx(
+            inner,
+            [&](auto outIdx)
+            {
+                auto const inIdx = outIdx + halo;
+                T want = hin[inIdx] + 42;
+                for(uint32_t d = 0u; d < extentMd.dim(); ++d)
+                {
+                    auto neg = inIdx;
+                    auto pos = inIdx;
+                    --neg[d];
+                    ++pos[d];
+                    want += hin[neg] * 3;
+                    want += hin[pos] * 5;
+                }
+                if(hout[outIdx] != want && bad++ < 3)
+                    expect(false, "cross stencil", hout[outIdx], want);
+            });
     }
 } // namespace
 
@@ -403,6 +631,24 @@ int main()
     transformTests(dev, queue, exec, Vec{7, 3});
     transformTests(dev, queue, exec, Vec{3});
     transformLarge(dev, queue, exec);
+    // extents of test/unit/algorithm/transformReduce.cpp:254-255 and concurrent.cpp
+    transformReducePins(dev, queue, exec, Vec{5, 7, 3, 11});
+    transformReducePins(dev, queue, exec, Vec{93, 7, 123});
+    transformReducePins(dev, queue, exec, Vec{5, 7, 4111});
+    transformReducePins(dev, queue, exec, Vec{5, 7, 3});
+    transformReducePins(dev, queue, exec, Vec{7, 3});
+    transformReducePins(dev, queue, exec, Vec{3});
+    concurrentPins(dev, queue, exec, Vec{5, 7, 3, 11});
+    concurrentPins(dev, queue, exec, Vec{93, 7, 123});
+    concurrentPins(dev, queue, exec, Vec{5, 7, 4111});
+    concurrentPins(dev, queue, exec, Vec{5, 7, 3});
+    concurrentPins(dev, queue, exec, Vec{7, 3});
+    concurrentPins(dev, queue, exec, Vec{3});
+    // test/unit/algorithm/transform.cpp:399-405
+    crossStencilOne(dev, queue, exec, Vec{17});
+    crossStencilOne(dev, queue, exec, Vec{17, 19});
+    crossStencilOne(dev, queue, exec, Vec{13, 17, 19});
+    crossStencilOne(dev, queue, exec, Vec{7, 11, 13, 17});
     // extents of test/unit/algorithm/iota.cpp:112-113
     auto const routedBeforeIota = alpaka3_b200::routingStats().routed.load();
     iotaOne(dev, queue, exec, Vec{5, 7, 3, 11});
@@ -415,7 +661,7 @@ int main()
                 static_cast<unsigned long long>(alpaka3_b200::routingStats().routed.load() - routedBeforeIota));
     auto& st = alpaka3_b200::routingStats();
     if(failures == 0)
-        std::printf("PASS routed=%llu forwarded=%llu\n", static_cast<unsigned long long>(st.routed.load()),
-                    static_cast<unsigned long long>(st.forwarded.load()));
+        std::printf("PASS routed=%llu engine=%llu forwarded=%llu\n", static_cast<unsigned long long>(st.routed.load()),
+                    static_cast<unsigned long long>(st.engine.load()), static_cast<unsigned long long>(st.forwarded.load()));
     return failures == 0 ? 0 : 1;
 }
