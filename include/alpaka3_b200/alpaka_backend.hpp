@@ -48,6 +48,7 @@
 #include <optional>
 #include <stdexcept>
 #include <string>
+#include <string_view>
 #include <type_traits>
 #include <utility>
 
@@ -108,6 +109,67 @@ namespace alpaka3_b200
 
     template<typename F>
     struct TransformKind<alpaka::ScalarFunc<F>> : TransformKind<F>
+    {
+    };
+
+    namespace detail
+    {
+        template<typename T>
+        constexpr std::string_view prettyName()
+        {
+            return __PRETTY_FUNCTION__;
+        }
+
+        constexpr bool identChar(char c)
+        {
+            return (c >= 'a' && c <= 'z') || (c >= 'A' && c <= 'Z') || (c >= '0' && c <= '9') || c == '_';
+        }
+
+        //! true when `name` occurs as a whole identifier in the compiler's spelling of T
+        template<typename T>
+        constexpr bool typeNamed(std::string_view name)
+        {
+            std::string_view const p = prettyName<T>();
+            for(auto pos = p.find(name); pos != std::string_view::npos; pos = p.find(name, pos + 1))
+            {
+                bool const before = pos == 0 || !identChar(p[pos - 1]);
+                bool const after = pos + name.size() >= p.size() || !identChar(p[pos + name.size()]);
+                if(before && after)
+                    return true;
+            }
+            return false;
+        }
+
+        template<typename K>
+        constexpr bool listedSimdForEachKernel()
+        {
+#if defined(ALPAKA3_B200_SIMD_FOR_EACH_KERNELS)
+            std::string_view list = ALPAKA3_B200_SIMD_FOR_EACH_KERNELS;
+            while(!list.empty())
+            {
+                auto const sp = list.find(' ');
+                std::string_view const tok = list.substr(0, sp);
+                if(!tok.empty() && typeNamed<K>(tok))
+                    return true;
+                if(sp == std::string_view::npos)
+                    break;
+                list.remove_prefix(sp + 1);
+            }
+#endif
+            return false;
+        }
+    } // namespace detail
+
+    /** Kernel types K whose body is exactly
+     *      onAcc::SimdAlgo{onAcc::worker::threadsInGrid}.concurrent(acc, arg0.getExtents(), op, arg0, args...)
+     * for a bundle KernelBundle{K{}, op, arg0, args...} -- BabelStream's SimdForEachKernel
+     * (benchmark/babelstream/src/babelStreamMainTest.cpp:61-75). queue.enqueue(FrameSpec, bundle) of such a kernel
+     * on a CUDA queue runs the bundle's op on the B200 SIMD engine instead of the kernel body (same op calls, the
+     * engine's grid). The binding cannot see a kernel's body, so this is opt-in: specialise the trait, or list the
+     * kernel type names (space separated) in the compile definition ALPAKA3_B200_SIMD_FOR_EACH_KERNELS, e.g.
+     * -DALPAKA3_B200_SIMD_FOR_EACH_KERNELS='"SimdForEachKernel"', which leaves the caller's source unchanged. */
+    template<typename K>
+    struct IsSimdForEachKernel : std::bool_constant<detail::listedSimdForEachKernel<K>()>
     {
     };
 
@@ -997,3 +1059,53 @@ namespace alpaka::onHost
             ALPAKA_FORWARD(inOut)...);
     }
 } // namespace alpaka::onHost
+
+#if defined(__CUDACC__)
+namespace alpaka::onHost::internal
+{
+    // queue.enqueue(FrameSpec, KernelBundle{K{}, op, arg0, args...}) of a SIMD for-each kernel (see
+    // alpaka3_b200::IsSimdForEachKernel) on a CUDA queue: the op runs on the B200 SIMD engine over arg0's extents, in
+    // place of alpaka3's own launch (include/alpaka/api/unifiedCudaHip/Queue.hpp:441-460).
+    template<
+        typename T_Device,
+        alpaka::concepts::UnifiedCudaHipExecutor T_Executor,
+        typename T_NumFrames,
+        typename T_FrameExtents,
+        typename K,
+        typename Op,
+        typename A0,
+        typename... A>
+    requires(alpaka3_b200::IsSimdForEachKernel<std::decay_t<K>>::value)
+    struct Enqueue::Kernel<
+        unifiedCudaHip::Queue<T_Device>,
+        FrameSpec<T_NumFrames, T_FrameExtents, T_Executor>,
+        KernelBundle<K, Op, A0, A...>>
+    {
+        void operator()(
+            unifiedCudaHip::Queue<T_Device>& queue,
+            FrameSpec<T_NumFrames, T_FrameExtents, T_Executor> const&,
+            KernelBundle<K, Op, A0, A...> const& bundle) const
+        {
+            using TApi = ALPAKA_TYPEOF(alpaka::internal::getApi(queue));
+            using TDeviceKind = ALPAKA_TYPEOF(queue.getDeviceKind());
+            auto const stream = static_cast<cudaStream_t>(queue.getNativeHandle());
+            alpaka::apply(
+                [&](auto const& op, auto const& arg0, auto const&... args)
+                {
+                    alpaka3_b200::detail::engineCheck(
+                        alpaka3_b200::simd::each<TApi, TDeviceKind, T_Executor>(
+                            stream,
+                            arg0.getExtents(),
+                            alpaka3_b200::simd::AccFirstBody<std::decay_t<decltype(op)>>{op},
+                            arg0,
+                            args...),
+                        "alpaka3_b200 SIMD for-each kernel");
+                },
+                bundle.m_args);
+            queue.conditionalWait();
+            ++alpaka3_b200::routingStats().routed;
+            ++alpaka3_b200::routingStats().engine;
+        }
+    };
+} // namespace alpaka::onHost::internal
+#endif

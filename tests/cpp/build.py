@@ -22,6 +22,8 @@ def build(force=False, reference_root=None):
         return OUT
     os.makedirs(os.path.dirname(OUT), exist_ok=True)
     cmd = ["nvcc", "-x", "cu", "-std=c++20", "-O2", "--expt-relaxed-constexpr", "--extended-lambda",
+           # the benchmark's SIMD for-each kernel runs on the B200 SIMD engine (alpaka3_b200::IsSimdForEachKernel)
+           '-DALPAKA3_B200_SIMD_FOR_EACH_KERNELS="SimdForEachKernel"',
            "-gencode", "arch=compute_100a,code=sm_100a", "-I" + os.path.join(root, "include"),
            "-I" + os.path.join(ROOT, "include"), src, "-o", OUT + ".tmp", "-L" + os.path.dirname(lib), "-lalpaka3_b200",
            "-Xlinker", "-rpath", "-Xlinker", "$ORIGIN/../../../alpaka3_b200/lib"]

@@ -509,6 +509,132 @@ namespace
         }
     };
 
+    // BabelStream's kernel and ops in the benchmark's form (benchmark/babelstream/src/babelStreamMainTest.cpp:61-141):
+    // enqueued with queue.enqueue(FrameSpec, KernelBundle{SimdForEachKernel{}, op, a, b, c}). The build lists
+    // SimdForEachKernel in ALPAKA3_B200_SIMD_FOR_EACH_KERNELS, so these launches run on the SIMD engine.
+    constexpr double kInitA = 0.1, kInitB = 0.2, kInitC = 0.0, kScalar = 0.4;
+
+    struct CopyOpLike
+    {
+    };
+
+    struct SimdForEachKernel
+    {
+        ALPAKA_FN_ACC void operator()(
+            auto const& acc,
+            auto const& func,
+            alpaka::concepts::IDataSource auto arg0,
+            alpaka::concepts::IDataSource auto... args) const
+        {
+            auto simdGrid = onAcc::SimdAlgo{onAcc::worker::threadsInGrid};
+            simdGrid.concurrent(acc, arg0.getExtents(), func, arg0, args...);
+        }
+    };
+
+    static_assert(alpaka3_b200::IsSimdForEachKernel<SimdForEachKernel>::value, "listed at compile time");
+    static_assert(!alpaka3_b200::IsSimdForEachKernel<CopyOpLike>::value, "not listed");
+
+    struct InitOp
+    {
+        constexpr void operator()(auto const&, auto a, auto b, auto c) const
+        {
+            using S = ALPAKA_TYPEOF(a.load());
+            a = S::fill(kInitA);
+            b = S::fill(kInitB);
+            c = S::fill(kInitC);
+        }
+    };
+
+    struct CopyOp
+    {
+        constexpr void operator()(auto const&, auto const a, auto c) const
+        {
+            c = a.load();
+        }
+    };
+
+    struct MulOp
+    {
+        constexpr void operator()(auto const&, auto b, auto const c) const
+        {
+            using T = trait::GetValueType_t<ALPAKA_TYPEOF(b)>;
+            b = static_cast<T>(kScalar) * c.load();
+        }
+    };
+
+    struct AddOp
+    {
+        constexpr void operator()(auto const&, auto const a, auto b, auto c) const
+        {
+            c = a.load() + b.load();
+        }
+    };
+
+    struct TriadOp
+    {
+        constexpr void operator()(auto const&, auto a, auto const b, auto const c) const
+        {
+            using T = trait::GetValueType_t<ALPAKA_TYPEOF(a)>;
+            a = b.load() + static_cast<T>(kScalar) * c.load();
+        }
+    };
+
+    struct NStreamOp
+    {
+        constexpr void operator()(auto const&, auto a, auto const b, auto const c) const
+        {
+            using T = trait::GetValueType_t<ALPAKA_TYPEOF(a)>;
+            a = a.load() + b.load() + static_cast<T>(kScalar) * c.load();
+        }
+    };
+
+    //! the benchmark's run sequence (init; runs x copy, mul, add, triad, dot; then nstream) against the uniform
+    //! values the host computes; counts the launches that ran on the engine
+    template<typename T>
+    void babelStreamKernels(auto& dev, auto& queue, auto exec, std::uint32_t n, int runs, double tol)
+    {
+        auto a = onHost::alloc<T>(dev, n);
+        auto b = onHost::allocLike(dev, a);
+        auto c = onHost::allocLike(dev, a);
+        auto frames = onHost::FrameSpec{(n + 512u * 8u - 1u) / (512u * 8u), 512u, exec};
+        auto const before = alpaka3_b200::routingStats().engine.load();
+        queue.enqueue(frames, KernelBundle{SimdForEachKernel{}, InitOp{}, a, b, c});
+        T ha = static_cast<T>(kInitA), hb = static_cast<T>(kInitB), hc = static_cast<T>(kInitC);
+        T const s = static_cast<T>(kScalar);
+        auto out = onHost::alloc<T>(dev, std::uint32_t{1});
+        auto hout = onHost::allocHostLike(out);
+        for(int r = 0; r < runs; ++r)
+        {
+            queue.enqueue(frames, KernelBundle{SimdForEachKernel{}, CopyOp{}, a, c});
+            queue.enqueue(frames, KernelBundle{SimdForEachKernel{}, MulOp{}, b, c});
+            queue.enqueue(frames, KernelBundle{SimdForEachKernel{}, AddOp{}, a, b, c});
+            queue.enqueue(frames, KernelBundle{SimdForEachKernel{}, TriadOp{}, a, b, c});
+            hc = ha;
+            hb = s * hc;
+            hc = ha + hb;
+            ha = hb + s * hc;
+        }
+        onHost::transformReduce(queue, exec, T{0}, out, std::plus{}, DotMultiplication{}, a, b);
+        queue.enqueue(frames, KernelBundle{SimdForEachKernel{}, NStreamOp{}, a, b, c});
+        T const dotWant = static_cast<T>(n) * ha * hb;
+        ha = ha + hb + s * hc;
+        auto h = onHost::allocHostLike(a);
+        onHost::memcpy(queue, hout, out);
+        onHost::memcpy(queue, h, a);
+        onHost::wait(queue);
+        expect(
+            alpaka3_b200::routingStats().engine.load() - before == static_cast<std::uint64_t>(2 + 4 * runs + 1),
+            "babelstream kernels on the engine",
+            static_cast<long long>(alpaka3_b200::routingStats().engine.load() - before),
+            2 + 4 * runs + 1);
+        std::size_t bad = 0;
+        for(auto const& v : h)
+            bad += std::abs(static_cast<double>(v) - static_cast<double>(ha)) > tol * std::abs(static_cast<double>(ha));
+        expect(bad == 0, "babelstream a after nstream", static_cast<long long>(bad), 0);
+        expect(std::abs(static_cast<double>(*hout.data()) - static_cast<double>(dotWant)) <= tol * std::abs(static_cast<double>(dotWant)),
+               "babelstream dot", 0, 0);
+    }
+
     //! concurrent<int>(extents, fn, a, b) with a = b = iota; a must become want(i, i)
     void concurrentOne(auto& dev, auto& queue, auto exec, auto extents, auto fn, auto want, char const* what)
     {
@@ -644,6 +770,9 @@ int main()
     concurrentPins(dev, queue, exec, Vec{5, 7, 3});
     concurrentPins(dev, queue, exec, Vec{7, 3});
     concurrentPins(dev, queue, exec, Vec{3});
+    // BabelStream through queue.enqueue: 2^18 elements (the benchmark's minimum array size), 10 runs
+    babelStreamKernels<double>(dev, queue, exec, 1u << 18, 10, 1e-12);
+    babelStreamKernels<float>(dev, queue, exec, (1u << 18) + 3u, 10, 1e-5);
     // test/unit/algorithm/transform.cpp:399-405
     crossStencilOne(dev, queue, exec, Vec{17});
     crossStencilOne(dev, queue, exec, Vec{17, 19});
