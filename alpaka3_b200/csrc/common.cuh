@@ -206,6 +206,77 @@ namespace a3b
         __stcs(p, v);
     }
 
+    // ------------------------------------------------------------------------------ TMA bulk copy + mbarrier
+    __device__ __forceinline__ uint32_t smemAddr(void const* p)
+    {
+        return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+    }
+
+    __device__ __forceinline__ void mbarInit(uint32_t bar, unsigned count)
+    {
+        asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+    }
+
+    // global -> shared bulk copy of `bytes`, completing on `bar` (16-byte aligned addresses and size)
+    __device__ __forceinline__ void bulkLoad(uint32_t dst, void const* src, unsigned bytes, uint32_t bar)
+    {
+        asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+        asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+             ::"r"(dst), "l"(src), "r"(bytes), "r"(bar)
+             : "memory");
+    }
+
+    // shared -> global bulk copy of `bytes` (16-byte aligned addresses and size), one bulk group
+    __device__ __forceinline__ void bulkStore(void* dst, uint32_t src, unsigned bytes)
+    {
+        asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(dst), "r"(src), "r"(bytes)
+             : "memory");
+        asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+    }
+
+    // wait until all but the newest `N` bulk groups have finished reading shared memory
+    template<int N>
+    __device__ __forceinline__ void bulkWaitRead()
+    {
+        asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+    }
+
+    __device__ __forceinline__ void bulkWaitAll()
+    {
+        asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+    }
+
+    __device__ __forceinline__ bool mbarTryWait(uint32_t bar, unsigned parity)
+    {
+        unsigned done;
+        asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(done)
+        : "r"(bar), "r"(parity)
+        : "memory");
+        return done != 0u;
+    }
+
+    // Bounded wait for the phase with `parity` of `bar`. A copy that never completes (it cannot, short of a
+    // fault) is reported in the error word; the wait is then repeated once, so that the block does not leave
+    // while the copy may still write its shared memory.
+    __device__ inline void mbarWait(uint32_t bar, unsigned parity, uint64_t timeoutNs, unsigned* errWord)
+    {
+        for(int attempt = 0; attempt < 2; ++attempt)
+        {
+        uint64_t const t0 = globalTimerNs();
+        while(!mbarTryWait(bar, parity))
+            if(globalTimerNs() - t0 > timeoutNs)
+            break;
+        if(mbarTryWait(bar, parity))
+            return;
+        if(attempt == 0 && (threadIdx.x & 31) == 0)
+            atomicOr(errWord, kErrTimeout);
+        }
+    }
+
     // ---------------------------------------------------------------------------------------------- Philox
     // Philox4x32-10 (Salmon et al., SC'11): counter (i_lo, i_hi, 0, 0), key (seed_lo, seed_hi)
     __host__ __device__ __forceinline__ uint4 philox4x32_10(uint64_t seed, uint64_t i)

@@ -130,6 +130,122 @@ namespace a3b
             }
         }
 
+        // ------------------------------------------------------------------ rows streamed through a shared ring
+        // The same march with the loads taken off the threads: each block owns a strip of kStrip storage columns of a
+        // band of kRingBand rows; thread 0 copies every row segment the band needs (the strip plus two columns on
+        // each side, 16-byte aligned) from HBM into a ring of kStages shared-memory slots with cp.async.bulk, a few
+        // rows ahead of the threads (own-GPU memory only, no multicast), and refills a slot as soon as every thread
+        // has read it. The threads keep north / centre in registers, take the south row and the warp-edge
+        // neighbours from shared memory and the other neighbours by shuffles, and store straight to HBM. The loads in
+        // flight no longer occupy registers, so the copy depth is set by the ring (kStages - 2 rows of 4 KB per block)
+        // rather than by the registers that limited the register-window march.
+        constexpr int kRingThreads = 256;
+        constexpr int kStrip = 2 * kRingThreads; // storage columns computed per block
+        constexpr int kSlot = kStrip + 4;        // doubles per ring slot: the strip and two columns each side
+        // Measured at 32768^2 (5 interleaved rounds, medians, GB/s of 16 B per cell): 10 stages x 32-row bands 6551
+        // (kept), 8 x 64 6425, 12 x 64 6438, 8 x 128 6331, 128-thread strips with 12 x 32 6315; the register-window
+        // march (heatKernelVec) ran 6114-6161.
+        constexpr int kStages = 10;
+        constexpr int kRingBand = 32;
+        constexpr size_t kRingSmem = static_cast<size_t>(kStages) * kSlot * sizeof(double);
+
+        __global__ void __launch_bounds__(kRingThreads) heatKernelRing(
+            double const* __restrict__ cur,
+            double* __restrict__ next,
+            uint64_t cols,
+            uint64_t pitch,
+            uint64_t rowBegin,
+            uint64_t rowEnd,
+            double rX,
+            double rY,
+            uint64_t timeoutNs,
+            unsigned* errWord)
+        {
+            extern __shared__ __align__(128) double ring[]; // kStages slots of kSlot doubles
+            __shared__ __align__(8) unsigned long long bar[kStages];
+            uint64_t const rb = rowBegin + static_cast<uint64_t>(blockIdx.y) * kRingBand;
+            if(rb >= rowEnd)
+                return;
+            uint64_t const re = rb + kRingBand < rowEnd ? rb + kRingBand : rowEnd;
+            uint64_t const width = cols + 2u;                             // storage columns (even here)
+            uint64_t const s0 = static_cast<uint64_t>(blockIdx.x) * kStrip; // first storage column of the strip
+            uint64_t const lo = s0 >= 2u ? s0 - 2u : 0u;                  // first column copied (even)
+            uint64_t const hi = s0 + kStrip + 2u < width ? s0 + kStrip + 2u : width; // one past the last (even)
+            unsigned const bytes = static_cast<unsigned>((hi - lo) * sizeof(double));
+            unsigned const dstOff = static_cast<unsigned>(lo + 2u - s0);   // slot index of column lo (0 or 2)
+            uint64_t const first = rb - 1u;                                // first row copied (north of rb)
+
+            auto slot = [&](uint64_t q) { return ring + ((q - first) % kStages) * kSlot; };
+            auto barOf = [&](uint64_t q) { return smemAddr(&bar[(q - first) % kStages]); };
+            auto parity = [&](uint64_t q) { return static_cast<unsigned>(((q - first) / kStages) & 1u); };
+            auto issue = [&](uint64_t q) { bulkLoad(smemAddr(slot(q) + dstOff), cur + q * pitch + lo, bytes, barOf(q)); };
+
+            if(threadIdx.x == 0)
+            {
+                for(int k = 0; k < kStages; ++k)
+                    mbarInit(smemAddr(&bar[k]), 1u);
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                for(uint64_t q = first; q < first + kStages && q <= re; ++q)
+                    issue(q);
+            }
+            __syncthreads();
+
+            int const lane = threadIdx.x & 31;
+            uint64_t const c0 = s0 + 2u * threadIdx.x; // storage columns c0, c0 + 1 of this thread
+            bool const live = c0 < width;
+            int const i0 = 2 + 2 * static_cast<int>(threadIdx.x); // slot index of c0
+            double const k = __dsub_rn(__dsub_rn(1.0, __dmul_rn(2.0, rX)), __dmul_rn(2.0, rY));
+            auto pairAt = [&](uint64_t q) { return *reinterpret_cast<double2 const*>(slot(q) + i0); };
+
+            mbarWait(barOf(first), parity(first), timeoutNs, errWord);
+            double2 up = pairAt(first);
+            mbarWait(barOf(rb), parity(rb), timeoutNs, errWord);
+            double2 mid = pairAt(rb);
+            __syncthreads(); // the slot of row rb - 1 is free
+            if(threadIdx.x == 0 && first + kStages <= re)
+            {
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                issue(first + kStages);
+            }
+            for(uint64_t r = rb; r < re; ++r)
+            {
+                mbarWait(barOf(r + 1u), parity(r + 1u), timeoutNs, errWord);
+                double2 const dn = pairAt(r + 1u);
+                double const* const cs = slot(r);
+                double westOfLo = __shfl_up_sync(0xffffffffu, mid.y, 1);
+                double eastOfHi = __shfl_down_sync(0xffffffffu, mid.x, 1);
+                if(lane == 0)
+                    westOfLo = cs[i0 - 1];
+                if(lane == 31)
+                    eastOfHi = cs[i0 + 2];
+                if(live)
+                {
+                    double* const q = next + r * pitch + c0;
+                    bool const loIn = c0 >= 1u && c0 <= cols;
+                    bool const hiIn = c0 + 1u <= cols;
+                    double const vlo = cell(mid.x, westOfLo, mid.y, up.x, dn.x, k, rX, rY);
+                    double const vhi = cell(mid.y, mid.x, eastOfHi, up.y, dn.y, k, rX, rY);
+                    if(loIn && hiIn)
+                        __stcs(reinterpret_cast<double2*>(q), make_double2(vlo, vhi));
+                    else
+                    {
+                        if(loIn)
+                            q[0] = vlo;
+                        if(hiIn)
+                            q[1] = vhi;
+                    }
+                }
+                up = mid;
+                mid = dn;
+                __syncthreads(); // every thread is done with the slot of row r
+                if(threadIdx.x == 0 && r + kStages <= re)
+                {
+                    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                    issue(r + kStages);
+                }
+            }
+        }
+
         // rows [rowBegin, rowEnd) of the interior, one band of kBand rows per blockIdx.y
         __global__ void __launch_bounds__(kThreads) heatKernelVec(
             double const* __restrict__ cur,
@@ -446,7 +562,24 @@ extern "C"
         uint64_t const bands = (row_end - row_begin + kBand - 1) / kBand;
         A3B_REQUIRE(bands < 65536u, "too many row bands");
         bool const vec = aligned16(cur) && aligned16(next) && pitch_elems % 2u == 0u;
-        if(vec)
+        if(vec && cols % 2u == 0u)
+        {
+            // even storage width: every copied row segment is a whole number of 16-byte units
+            static std::atomic<int> attrSet[kMaxDevices] = {};
+            if(!attrSet[props->ordinal].load(std::memory_order_relaxed))
+            {
+                A3B_CUDA(cudaFuncSetAttribute(heatKernelRing, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                              static_cast<int>(kRingSmem)));
+                attrSet[props->ordinal].store(1, std::memory_order_relaxed);
+            }
+            uint64_t const ringBands = (row_end - row_begin + kRingBand - 1) / kRingBand;
+            uint64_t const strips = (cols + 2u + kStrip - 1) / kStrip;
+            A3B_REQUIRE(ringBands < 65536u, "too many row bands");
+            dim3 const grid(static_cast<unsigned>(strips), static_cast<unsigned>(ringBands));
+            heatKernelRing<<<grid, kRingThreads, kRingSmem, s>>>(cur, next, cols, pitch_elems, row_begin, row_end, rX,
+                                                                 rY, waitTimeoutNs(), props->errWord);
+        }
+        else if(vec)
         {
             uint64_t const packs = (cols + 2u + 1u) / 2u;
             dim3 const grid(static_cast<unsigned>((packs + kThreads - 1) / kThreads), static_cast<unsigned>(bands));
