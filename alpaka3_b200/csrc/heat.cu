@@ -149,24 +149,22 @@ namespace a3b
         constexpr int kRingBand = 32;
         constexpr size_t kRingSmem = static_cast<size_t>(kStages) * kSlot * sizeof(double);
 
-        __global__ void __launch_bounds__(kRingThreads) heatKernelRing(
+        // Rows [rb, re) of the strip of block x, streamed through the ring (`ring`: kStages slots of kSlot doubles,
+        // `bar`: kStages mbarriers, both in shared memory). Rows rb - 1 .. re of `cur` are read.
+        __device__ __forceinline__ void ringBand(
             double const* __restrict__ cur,
             double* __restrict__ next,
             uint64_t cols,
             uint64_t pitch,
-            uint64_t rowBegin,
-            uint64_t rowEnd,
+            uint64_t rb,
+            uint64_t re,
             double rX,
             double rY,
             uint64_t timeoutNs,
-            unsigned* errWord)
+            unsigned* errWord,
+            double* ring,
+            unsigned long long* bar)
         {
-            extern __shared__ __align__(128) double ring[]; // kStages slots of kSlot doubles
-            __shared__ __align__(8) unsigned long long bar[kStages];
-            uint64_t const rb = rowBegin + static_cast<uint64_t>(blockIdx.y) * kRingBand;
-            if(rb >= rowEnd)
-                return;
-            uint64_t const re = rb + kRingBand < rowEnd ? rb + kRingBand : rowEnd;
             uint64_t const width = cols + 2u;                             // storage columns (even here)
             uint64_t const s0 = static_cast<uint64_t>(blockIdx.x) * kStrip; // first storage column of the strip
             uint64_t const lo = s0 >= 2u ? s0 - 2u : 0u;                  // first column copied (even)
@@ -244,6 +242,27 @@ namespace a3b
                     issue(r + kStages);
                 }
             }
+        }
+
+        __global__ void __launch_bounds__(kRingThreads) heatKernelRing(
+            double const* __restrict__ cur,
+            double* __restrict__ next,
+            uint64_t cols,
+            uint64_t pitch,
+            uint64_t rowBegin,
+            uint64_t rowEnd,
+            double rX,
+            double rY,
+            uint64_t timeoutNs,
+            unsigned* errWord)
+        {
+            extern __shared__ __align__(128) double ring[]; // kStages slots of kSlot doubles
+            __shared__ __align__(8) unsigned long long bar[kStages];
+            uint64_t const rb = rowBegin + static_cast<uint64_t>(blockIdx.y) * kRingBand;
+            if(rb >= rowEnd)
+                return;
+            uint64_t const re = rb + kRingBand < rowEnd ? rb + kRingBand : rowEnd;
+            ringBand(cur, next, cols, pitch, rb, re, rX, rY, timeoutNs, errWord, ring, bar);
         }
 
         // rows [rowBegin, rowEnd) of the interior, one band of kBand rows per blockIdx.y
@@ -378,6 +397,75 @@ namespace a3b
                 return;
             uint64_t const rb = 1u + band * kBand;
             uint64_t const re = rb + kBand < rows + 1u ? rb + kBand : rows + 1u;
+            bool const top = rb == 1u, bottom = re == rows + 1u;
+            unsigned const rd = (step - 1u) & 1u, wr = step & 1u;
+            double const* north = nullptr;
+            double const* south = nullptr;
+            if(top && up.rows)
+            {
+                if(!waitFlag(mine.flag(0, rd, blockIdx.x), step, timeoutNs, errWord))
+                    return;
+                north = mine.row(0, rd);
+            }
+            if(bottom && down.rows)
+            {
+                if(!waitFlag(mine.flag(1, rd, blockIdx.x), step, timeoutNs, errWord))
+                    return;
+                south = mine.row(1, rd);
+            }
+            heatBand(cur, next, cols, pitch, rb, re, rX, rY, rows, north, south);
+            if(top && up.rows)
+            {
+                __syncthreads(); // the block's row 1 is in `next`
+                sendRow(next + pitch, cols, up.row(1, wr), up.flag(1, wr, blockIdx.x), step + 1u);
+            }
+            if(bottom && down.rows)
+            {
+                __syncthreads();
+                sendRow(next + rows * pitch, cols, down.row(0, wr), down.flag(0, wr, blockIdx.x), step + 1u);
+            }
+        }
+
+        // The same step with the interior on the shared-memory ring (even storage widths): blockIdx.y = 0 is the first
+        // band of kBand rows, 1 the last band (both on the register march, which takes its ghost rows from the
+        // mailbox), the others the interior rows between them in bands of kRingBand rows streamed through the ring.
+        __global__ void __launch_bounds__(kThreads) heatExchangeRingKernel(
+            double const* __restrict__ cur,
+            double* __restrict__ next,
+            uint64_t rows,
+            uint64_t cols,
+            uint64_t pitch,
+            double rX,
+            double rY,
+            Mail mine,
+            Mail up,
+            Mail down,
+            unsigned step,
+            uint64_t timeoutNs,
+            unsigned* errWord)
+        {
+            extern __shared__ __align__(128) double ring[];
+            __shared__ __align__(8) unsigned long long bar[kStages];
+            uint64_t const topEnd = 1u + kBand < rows + 1u ? 1u + kBand : rows + 1u;
+            uint64_t const lastBegin = rows + 1u > kBand ? rows + 1u - kBand : 1u;
+            uint64_t const botBegin = lastBegin > topEnd ? lastBegin : topEnd;
+            if(blockIdx.y >= 2u)
+            {
+                uint64_t const rb = topEnd + static_cast<uint64_t>(blockIdx.y - 2u) * kRingBand;
+                if(rb >= botBegin)
+                    return;
+                uint64_t const re = rb + kRingBand < botBegin ? rb + kRingBand : botBegin;
+                ringBand(cur, next, cols, pitch, rb, re, rX, rY, timeoutNs, errWord, ring, bar);
+                return;
+            }
+            uint64_t rb = 1u, re = topEnd;
+            if(blockIdx.y == 1u)
+            {
+                if(botBegin >= rows + 1u)
+                    return; // one band holds every row: block y = 0 does it
+                rb = botBegin;
+                re = rows + 1u;
+            }
             bool const top = rb == 1u, bottom = re == rows + 1u;
             unsigned const rd = (step - 1u) & 1u, wr = step & 1u;
             double const* north = nullptr;
@@ -699,10 +787,33 @@ extern "C"
         uint64_t const bands = (rows + kBand - 1) / kBand;
         A3B_REQUIRE(bands < 65536u, "too many row bands");
         unsigned const step = ++h->step;
-        dim3 const grid(colBlocks, static_cast<unsigned>(bands));
-        heatExchangeKernel<<<grid, kThreads, 0, static_cast<cudaStream_t>(stream)>>>(
-            cur, next, rows, cols, pitch_elems, rX, rY, mailOf(h->local, cols), mailOf(h->up, cols),
-            mailOf(h->down, cols), step, waitTimeoutNs(), props->errWord);
+        if(cols % 2u == 0u)
+        {
+            // boundary bands of kBand rows, the interior in ring bands of kRingBand rows
+            static std::atomic<int> attrSet[kMaxDevices] = {};
+            if(!attrSet[props->ordinal].load(std::memory_order_relaxed))
+            {
+                A3B_CUDA(cudaFuncSetAttribute(heatExchangeRingKernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                              static_cast<int>(kRingSmem)));
+                attrSet[props->ordinal].store(1, std::memory_order_relaxed);
+            }
+            uint64_t const topEnd = 1u + kBand < rows + 1u ? 1u + kBand : rows + 1u;
+            uint64_t const lastBegin = rows + 1u > kBand ? rows + 1u - kBand : 1u;
+            uint64_t const botBegin = lastBegin > topEnd ? lastBegin : topEnd;
+            uint64_t const inner = (botBegin - topEnd + kRingBand - 1) / kRingBand;
+            A3B_REQUIRE(inner + 2u < 65536u, "too many row bands");
+            dim3 const grid(colBlocks, static_cast<unsigned>(2u + inner));
+            heatExchangeRingKernel<<<grid, kThreads, kRingSmem, static_cast<cudaStream_t>(stream)>>>(
+                cur, next, rows, cols, pitch_elems, rX, rY, mailOf(h->local, cols), mailOf(h->up, cols),
+                mailOf(h->down, cols), step, waitTimeoutNs(), props->errWord);
+        }
+        else
+        {
+            dim3 const grid(colBlocks, static_cast<unsigned>(bands));
+            heatExchangeKernel<<<grid, kThreads, 0, static_cast<cudaStream_t>(stream)>>>(
+                cur, next, rows, cols, pitch_elems, rX, rY, mailOf(h->local, cols), mailOf(h->up, cols),
+                mailOf(h->down, cols), step, waitTimeoutNs(), props->errWord);
+        }
         A3B_CHECK_LAUNCH("heat halo step launch");
         return A3B_OK;
     }

@@ -103,3 +103,40 @@ def test_heat_example_problem_reference_golden(cuda):
     err = np.max(np.abs(u[1:-1, 1:-1] - exact[1:-1, 1:-1]))
     assert err < 1e-4
     assert abs(err - float(g["err"])) <= 1e-9
+
+
+@pytest.mark.parametrize("rows,cols,pad", [(1000, 1000, 0), (130, 64, 0), (64, 130, 0), (200, 999, 1), (7, 12, 0),
+                                           (97, 2046, 0)])
+def test_halo_step_one_rank_matches_plain_step(cuda, rows, cols, pad):
+    """The fused halo step (a3b_heat_step_halo) on a one-rank mailbox: the slab is the whole grid, so it must give the
+    plain stencil's bits step after step. Even widths run the boundary bands on the register march and the interior
+    on the shared-memory ring; odd widths (pitch padded to even) run the register march everywhere."""
+    import ctypes
+
+    from alpaka3_b200 import algo, capi
+    L = capi.lib()
+    pitch = cols + 2 + pad
+    store = torch.zeros((rows + 2, pitch), dtype=torch.float64, device=cuda)
+    u = store[:, :cols + 2]
+    dx = 1.0 / (cols + 1)
+    algo.heat_init(u, dx, 1.0 / (rows + 1))
+    a = [store.clone(), store.clone()]
+    b = [store.clone(), store.clone()]
+    handle = (ctypes.c_char * L.a3b_ipc_handle_size())()
+    h = ctypes.c_void_p()
+    capi.call("a3b_halo_create", 1, 0, cols, ctypes.byref(h), handle)
+    try:
+        capi.call("a3b_halo_connect", h, handle)
+        s = algo.stream_handle()
+        capi.call("a3b_heat_halo_publish", s, h, ctypes.c_void_p(a[0].data_ptr()), rows, cols, pitch)
+        for k in range(5):
+            src, dst = a[k % 2], a[(k + 1) % 2]
+            capi.call("a3b_heat_step_halo", s, h, ctypes.c_void_p(src.data_ptr()), ctypes.c_void_p(dst.data_ptr()),
+                      rows, cols, pitch, 0.2, 0.2)
+            algo.heat_step(b[k % 2][:, :cols + 2], b[(k + 1) % 2][:, :cols + 2], 0.2, 0.2)
+        torch.cuda.synchronize()
+        assert capi.device_error(s) == 0
+        assert torch.equal(a[1][1:rows + 1, :cols + 2], b[1][1:rows + 1, :cols + 2])
+    finally:
+        torch.cuda.synchronize()
+        capi.call("a3b_halo_destroy", h)
