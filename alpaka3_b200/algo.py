@@ -218,6 +218,12 @@ def nbody_step(m, x, y, z, vx, vy, vz, dt, eps, i_begin=0, stream=None):
 
 
 # -------------------------------------------------------------------------------------------------------- heat
+def haccmk_step10(xx, yy, zz, mass, vx2, vy2, vz2, n1, fsrrmax2, mp_rsm2, fcoeff, stream=None):
+    """HACCmk's Step10 short-range force for the first n1 particles against all of xx/yy/zz/mass (float32)."""
+    capi.call("a3b_haccmk_step10", stream_handle(stream), _ptr(xx), _ptr(yy), _ptr(zz), _ptr(mass), int(n1),
+              xx.numel(), float(fsrrmax2), float(mp_rsm2), float(fcoeff), _ptr(vx2), _ptr(vy2), _ptr(vz2))
+
+
 def heat_step(cur, nxt, rX, rY, row_begin=1, row_end=None, stream=None):
     """cur/nxt: (rows+2, cols+2) float64 tensors (rows may be pitched: stride(0) >= cols + 2)."""
     rows, cols = cur.shape[0] - 2, cur.shape[1] - 2

@@ -68,6 +68,7 @@ SIGNATURES = {
     "a3b_scan": [_P, _I, _I, _P, _P, _U64, _P, _P, ctypes.c_size_t],
     "a3b_nbody_update_velocities": [_P, _P, _P, _P, _P, _U64, _U64, _U64, _P, _P, _P, _F, _F],
     "a3b_nbody_step": [_P, _P, _P, _P, _P, _U64, _U64, _U64, _P, _P, _P, _F, _F],
+    "a3b_haccmk_step10": [_P, _P, _P, _P, _P, _I, _I, _F, _F, _F, _P, _P, _P],
     "a3b_heat_step": [_P, _P, _P, _U64, _U64, _U64, _U64, _U64, _D, _D],
     "a3b_heat_init": [_P, _P, _U64, _U64, _U64, _U64, _U64, _D, _D],
     "a3b_heat_exact": [_P, _P, _U64, _U64, _U64, _U64, _U64, _D, _D, _D, _I],

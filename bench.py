@@ -376,6 +376,22 @@ def bench_parts(torch, algo, dev, args, peak):
                                   "peak": "148 SMs x 128 FP32 lanes x 2 x 1.965 GHz = 74.4 TFLOP/s (nominal)"}
     del m, px, py, pz, v
 
+    # HACCmk short-range force at the benchmark's defaults (15000 particles, 784 active; benchmark/HACCmk/src/misc.hpp:
+    # 24-25): the benchmark reports the average kernel time
+    n2, n1 = 15000, 784
+    hx, hy, hz, hm = (torch.empty(n2, dtype=torch.float32, device=dev) for _ in range(4))
+    d1 = (1.0 / n2, 2.0 / n2, 3.0 / n2)
+    idx = torch.arange(n2, dtype=torch.float64, device=dev)
+    for t, d in zip((hx, hy, hz), d1):
+        t.copy_((idx * d).float())  # stand-in positions of the same spread (timing only; parity is in the tests)
+    hm.copy_((idx * 0.01).float() + hx)
+    hv = [torch.zeros(n1, dtype=torch.float32, device=dev) for _ in range(3)]
+    ms_h, _ = time_steps(torch, False, lambda ev: algo.haccmk_step10(hx, hy, hz, hm, *hv, n1, 0.5, 0.03, 0.23),
+                         max(args.steps, 20), max(args.warmup, 3), kernel_events=False)
+    parts["haccmk_15000x784_step10"] = {"us_per_call": round(ms_h * 1e3, 2),
+                                        "pairs_per_s": round(float(n1) * n2 / (ms_h * 1e-3), 1)}
+    del hx, hy, hz, hm, hv, idx
+
     # heat, 32768 x 32768 interior fp64 (8.6 GB per field), dt/dx^2 = 0.2
     side = 32768
     u = torch.empty((side + 2, side + 2), dtype=torch.float64, device=dev)

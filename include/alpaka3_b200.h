@@ -270,6 +270,17 @@ A3B_API int a3b_nbody_update_velocities(a3b_stream_t stream, float const* m, flo
 A3B_API int a3b_nbody_step(a3b_stream_t stream, float const* m, float* x, float* y, float* z, uint64_t n_all,
                    uint64_t i_begin, uint64_t i_count, float* vx, float* vy, float* vz, float dt, float eps);
 
+/* --------------------------------------------------------------------------------------------------- HACCmk */
+
+/* HACCmk's short-range force step (benchmark/HACCmk/src/main_alpaka.cpp:47-123 Step10Kernel, CPU gold
+ * helper.hpp:19-66): for the first n1 particles (targets) against all n2 particles (sources),
+ *   d = p_j - p_i, r2 = |d|^2, m = (r2 < fsrrmax2) ? mass_j : 0, f = r2 + mp_rsm2,
+ *   f = m * (1 / (f * sqrt f) - poly(r2)),  v_i = fcoeff * sum_j f * d   (written to vx2/vy2/vz2[i], i < n1).
+ * fp32, SoA; 0 <= n1 <= n2. */
+A3B_API int a3b_haccmk_step10(a3b_stream_t stream, float const* xx, float const* yy, float const* zz, float const* mass,
+                              int n1, int n2, float fsrrmax2, float mp_rsm2, float fcoeff, float* vx2, float* vy2,
+                              float* vz2);
+
 /* ------------------------------------------------------------------------------------------------------ heat */
 
 /* StencilKernel (example/heatEquation2D/src/StencilKernel.hpp:26-86): one explicit 5-point Jacobi step on a row-major

@@ -18,6 +18,7 @@ g++ -std=c++20 -O3 -march=x86-64-v3 -fopenmp -ffp-contract=off -fPIC -shared \
     -I"$REF/include" \
     -I"$REF/example/heatEquation2D/src" \
     -I"$REF/example/nBody/src" \
+    -I"$REF/benchmark/HACCmk/src" \
     -o "$OUT/libalpaka_ref.so.tmp" "$HERE/ref_harness.cpp"
 mv "$OUT/libalpaka_ref.so.tmp" "$OUT/libalpaka_ref.so"
 echo "built $OUT/libalpaka_ref.so"

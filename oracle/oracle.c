@@ -401,6 +401,56 @@ void orc_nbody_accel_sample(
     }
 }
 
+/* ----------------------------------------------------------------------------------------------------- HACCmk */
+
+/* The benchmark's input (benchmark/HACCmk/src/main_alpaka.cpp:254-272): positions advanced by fixed steps in fp32
+ * one particle after the other, masses i * 0.01 + x_i. */
+void orc_haccmk_init(int n2, float* xx, float* yy, float* zz, float* mass)
+{
+    float const dx1 = 1.0f / (float)n2, dy1 = 2.0f / (float)n2, dz1 = 3.0f / (float)n2;
+    xx[0] = 0.f;
+    yy[0] = 0.f;
+    zz[0] = 0.f;
+    mass[0] = 2.f;
+    for(int i = 1; i < n2; ++i)
+    {
+        xx[i] = xx[i - 1] + dx1;
+        yy[i] = yy[i - 1] + dy1;
+        zz[i] = zz[i - 1] + dz1;
+        mass[i] = (float)i * 0.01f + xx[i];
+    }
+}
+
+/* Short-range force of the first n1 particles against all n2, each target's pairs summed in source order, as the
+ * reference's CPU gold (helper.hpp:19-66) computes it; v = fcoeff * sum (main_alpaka.cpp:288-293). */
+void orc_haccmk_step10(int n1, int n2, float const* xx, float const* yy, float const* zz, float const* mass,
+                       float fsrrmax2, float mp_rsm2, float fcoeff, float* vx, float* vy, float* vz)
+{
+    float const ma0 = 0.269327f, ma1 = -0.0750978f, ma2 = 0.0114808f, ma3 = -0.00109313f, ma4 = 0.0000605491f,
+                ma5 = -0.00000147177f;
+#pragma omp parallel for schedule(static)
+    for(int i = 0; i < n1; ++i)
+    {
+        float sx = 0.f, sy = 0.f, sz = 0.f;
+        for(int j = 0; j < n2; ++j)
+        {
+            float const dxc = xx[j] - xx[i];
+            float const dyc = yy[j] - yy[i];
+            float const dzc = zz[j] - zz[i];
+            float const r2 = dxc * dxc + dyc * dyc + dzc * dzc;
+            float const m = r2 < fsrrmax2 ? mass[j] : 0.f;
+            float f = r2 + mp_rsm2;
+            f = m * (1.f / (f * sqrtf(f)) - (ma0 + r2 * (ma1 + r2 * (ma2 + r2 * (ma3 + r2 * (ma4 + r2 * ma5))))));
+            sx = sx + f * dxc;
+            sy = sy + f * dyc;
+            sz = sz + f * dzc;
+        }
+        vx[i] = 0.f + sx * fcoeff;
+        vy[i] = 0.f + sy * fcoeff;
+        vz[i] = 0.f + sz * fcoeff;
+    }
+}
+
 int orc_num_threads(void)
 {
 #ifdef _OPENMP

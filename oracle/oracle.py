@@ -62,6 +62,8 @@ class Port:
         L.orc_nbody_step.argtypes = [_P] * 7 + [_U64, ctypes.c_float, ctypes.c_float]
         L.orc_nbody_accel_sample.argtypes = [_P] * 4 + [_U64, ctypes.c_float, _P, _U64, _P]
         L.orc_philox.argtypes = [_U64, _U64, _P]
+        L.orc_haccmk_init.argtypes = [ctypes.c_int, _P, _P, _P, _P]
+        L.orc_haccmk_step10.argtypes = [ctypes.c_int, ctypes.c_int] + [_P] * 4 + [ctypes.c_float] * 3 + [_P] * 3
         L.orc_num_threads.restype = ctypes.c_int
 
     # ---- seeded inputs (Philox4x32-10, counter = element index) ----
@@ -157,6 +159,18 @@ class Port:
         self.lib.orc_nbody_accel_sample(_p(m), _p(x), _p(y), _p(z), m.size, eps, _p(idx), idx.size, _p(out))
         return out
 
+    def haccmk_init(self, n2):
+        """HACCmk's input (main_alpaka.cpp:254-272): xx, yy, zz, mass of n2 particles."""
+        arrs = [np.empty(n2, dtype=np.float32) for _ in range(4)]
+        self.lib.orc_haccmk_init(n2, *[_p(a) for a in arrs])
+        return arrs
+
+    def haccmk_step10(self, n1, xx, yy, zz, mass, fsrrmax2=0.5, mp_rsm2=0.03, fcoeff=0.23):
+        out = [np.zeros(n1, dtype=np.float32) for _ in range(3)]
+        self.lib.orc_haccmk_step10(n1, xx.size, _p(xx), _p(yy), _p(zz), _p(mass), fsrrmax2, mp_rsm2, fcoeff,
+                                   *[_p(a) for a in out])
+        return out
+
     def num_threads(self):
         return self.lib.orc_num_threads()
 
@@ -188,6 +202,14 @@ class Ref:
         L.ref_heat_problem.restype = ctypes.c_double
         L.ref_num_threads.restype = ctypes.c_int
         L.ref_set_num_threads.argtypes = [ctypes.c_int]
+        L.ref_haccmk_gold.argtypes = [ctypes.c_int, ctypes.c_int] + [_P] * 4 + [ctypes.c_float] * 3 + [_P] * 3
+
+    def haccmk_gold(self, n1, xx, yy, zz, mass, fsrrmax2=0.5, mp_rsm2=0.03, fcoeff=0.23):
+        """HACCmk's own CPU gold (helper.hpp) for the first n1 particles."""
+        out = [np.zeros(n1, dtype=np.float32) for _ in range(3)]
+        assert self.lib.ref_haccmk_gold(n1, xx.size, _p(xx), _p(yy), _p(zz), _p(mass), fsrrmax2, mp_rsm2, fcoeff,
+                                        *[_p(a) for a in out]) == 0
+        return out
 
     def set_num_threads(self, n):
         """OpenMP threads of alpaka3's host backend for every later call."""

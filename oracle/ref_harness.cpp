@@ -222,6 +222,8 @@ namespace
     }
 } // namespace
 
+#include "helper.hpp" // benchmark/HACCmk/src: the reference's CPU gold of the short-range force
+
 extern "C"
 {
     /** kernels bitmask: 1 copy, 2 mul, 4 add, 8 triad, 16 dot, 32 nstream. times: 5 doubles per run (or null). */
@@ -455,6 +457,22 @@ extern "C"
                     onHost::wait(q);
                 }
             });
+        return 0;
+    }
+
+    // HACCmk's CPU gold (benchmark/HACCmk/src/helper.hpp:19-66) for the first n1 particles, as the benchmark applies it
+    // (main_alpaka.cpp:288-293, velocities starting at 0)
+    int ref_haccmk_gold(int n1, int n2, float const* xx, float const* yy, float const* zz, float const* mass,
+                        float fsrrmax2, float mp_rsm2, float fcoeff, float* vx, float* vy, float* vz)
+    {
+        for(int i = 0; i < n1; ++i)
+        {
+            float dx2 = 0.f, dy2 = 0.f, dz2 = 0.f;
+            hacc::haccmk_gold(n2, xx[i], yy[i], zz[i], fsrrmax2, mp_rsm2, xx, yy, zz, mass, &dx2, &dy2, &dz2);
+            vx[i] = 0.f + dx2 * fcoeff;
+            vy[i] = 0.f + dy2 * fcoeff;
+            vz[i] = 0.f + dz2 * fcoeff;
+        }
         return 0;
     }
 

@@ -113,3 +113,15 @@ def test_heat_example_problem_golden(ref):
     u, err = ref.heat_problem(int(g["n"]), int(g["steps"]), float(g["t_max"]))
     assert (u == g["u"]).all()
     assert err < 1e-4 and err == float(g["err"])
+
+
+def test_haccmk_restatement_matches_reference_gold(port, ref):
+    """oracle.c's HACCmk step equals the benchmark's own CPU gold (benchmark/HACCmk/src/helper.hpp:19-66) bit for bit,
+    at the benchmark's default size (15000 particles, 784 active) and two others."""
+    import numpy as np
+    for n2, n1 in ((15000, 784), (1000, 1000), (4096, 100)):
+        xx, yy, zz, m = port.haccmk_init(n2)
+        a = port.haccmk_step10(n1, xx, yy, zz, m)
+        b = ref.haccmk_gold(n1, xx, yy, zz, m)
+        for x, y in zip(a, b):
+            assert (x.view(np.uint32) == y.view(np.uint32)).all()
