@@ -169,6 +169,18 @@ namespace a3b
         asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
     }
 
+    __device__ __forceinline__ unsigned long long ldAcquireU64(unsigned long long const* p)
+    {
+        unsigned long long v;
+        asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+        return v;
+    }
+
+    __device__ __forceinline__ void stReleaseU64(unsigned long long* p, unsigned long long v)
+    {
+        asm volatile("st.release.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+    }
+
     __device__ __forceinline__ unsigned ldAcquireU32(unsigned const* p)
     {
         unsigned v;

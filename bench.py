@@ -116,6 +116,24 @@ class ClockSampler:
                 "reasons": sorted(self.reasons - {"gpu_idle"}), "samples": len(self.samples)}
 
 
+def gpu_local_cpus(torch, ordinal):
+    """CPUs attached to the GPU's PCIe root (sysfs local_cpulist of its PCI device), or None."""
+    try:
+        bdf = pci_bus_id(torch, ordinal).lower()[4:]  # dddd:bb:dd.f
+        with open(f"/sys/bus/pci/devices/{bdf}/local_cpulist") as f:
+            text = f.read().strip()
+        cpus = set()
+        for part in text.split(","):
+            if "-" in part:
+                a, b = part.split("-")
+                cpus.update(range(int(a), int(b) + 1))
+            elif part:
+                cpus.add(int(part))
+        return cpus & set(os.sched_getaffinity(0)) or None
+    except (OSError, ValueError, AttributeError):
+        return None
+
+
 def pci_bus_id(torch, ordinal):
     p = torch.cuda.get_device_properties(ordinal)
     return "%08X:%02X:%02X.0" % (getattr(p, "pci_domain_id", 0), p.pci_bus_id, p.pci_device_id)
@@ -222,6 +240,12 @@ def run_b200(args):
     # ---------------------------------------------------------------- e2e: host buffers through the C ABI
     e2e = None
     if not args.no_e2e:
+        # pinned pages land on the NUMA node of the allocating thread: allocate (and touch) them from CPUs next to
+        # this rank's GPU, so the host->device copies do not cross the socket interconnect
+        local_cpus = gpu_local_cpus(torch, local)
+        saved_affinity = os.sched_getaffinity(0)
+        if local_cpus:
+            os.sched_setaffinity(0, local_cpus)
         host = torch.empty(n_local, dtype=torch.float32, pin_memory=True)
         host.copy_(x.cpu())
         res_host = torch.empty(1, dtype=torch.float64 if (dist_on and group is None) else torch.float32,
@@ -248,10 +272,21 @@ def run_b200(args):
         e_steps = max(1, min(args.steps, 10))
         e_ms, _ = time_steps(torch, dist_on, e2e_step, e_steps, 1, kernel_events=False)
         e_ms = max_over_ranks(torch, dist_on, e_ms)
+
+        def h2d_step(ev):
+            capi.call("a3b_memcpy_async", ctypes.c_void_p(x.data_ptr()), ctypes.c_void_p(host.data_ptr()),
+                      4 * n_local, sh)
+
+        h_ms, _ = time_steps(torch, dist_on, h2d_step, e_steps, 1, kernel_events=False)
+        h_worst = max_over_ranks(torch, dist_on, h_ms)
         e2e = {"value": total_bytes / (e_ms * 1e-3) / 1e9, "unit": "GB/s", "h2d_bytes_per_step": 4 * N_SUMSQ,
                "d2h_bytes_per_step": res_host.element_size() * world, "steps": e_steps,
-               "path": "a3b_memcpy_async(H2D, pinned) + a3b_transform_reduce + a3b_memcpy_async(D2H)"}
+               "path": "a3b_memcpy_async(H2D, pinned) + a3b_transform_reduce + a3b_memcpy_async(D2H)",
+               "h2d_only_GBps_all_ranks": round(total_bytes / (h_worst * 1e-3) / 1e9, 1),
+               "host_buffer": "pinned, allocated from the CPUs local to each rank's GPU" if local_cpus
+               else "pinned (GPU-local CPUs unknown)"}
         del host
+        os.sched_setaffinity(0, saved_affinity)
 
     # ---------------------------------------------------------------- other kernels of the metric
     del x
