@@ -38,7 +38,7 @@ namespace a3b
 
         // At least 8 resident blocks: measured 50.2 TFLOP/s (64 threads) against 45.9 without the bound at 262144
         // bodies; the compiler keeps more j-steps in flight.
-        template<int PAIRS, int THREADS>
+        template<int PAIRS, int THREADS, int JILP>
         __global__ void __launch_bounds__(THREADS, 8) forceKickKernel(
             float const* __restrict__ m,
             float const* __restrict__ x,
@@ -55,6 +55,7 @@ namespace a3b
         {
             constexpr int kIBlock = 2 * PAIRS * THREADS;
             constexpr int kUnroll = PAIRS == 1 ? 8 : 4;
+            static_assert(kJTile % JILP == 0 && kUnroll % JILP == 0, "j-steps must divide the tile and the unroll");
             __shared__ float4 sj[kJTile]; // {x, y, z, m} per j-body; one broadcast 16-byte load per j
             float2 const eps2 = make_float2(eps, eps);
 
@@ -90,30 +91,43 @@ namespace a3b
                     sj[t] = j < nAll ? make_float4(x[j], y[j], z[j], m[j]) : make_float4(kFar, kFar, kFar, 0.f);
                 }
                 __syncthreads();
-#pragma unroll kUnroll
-                for(int t = 0; t < kJTile; ++t)
+#pragma unroll(kUnroll / JILP)
+                for(int t = 0; t < kJTile; t += JILP)
                 {
-                    float4 const b = sj[t];
-                    float2 const bx = make_float2(b.x, b.x);
-                    float2 const by = make_float2(b.y, b.y);
-                    float2 const bz = make_float2(b.z, b.z);
-                    float2 const bm = make_float2(b.w, b.w);
+                    // the distance terms of JILP consecutive j-bodies are independent of each other and of the
+                    // sums; the sums then take them in index order
+                    float2 dx[JILP][PAIRS], dy[JILP][PAIRS], dz[JILP][PAIRS], sc[JILP][PAIRS];
 #pragma unroll
-                    for(int p = 0; p < PAIRS; ++p)
+                    for(int q = 0; q < JILP; ++q)
                     {
-                        float2 const dx = __fadd2_rn(bx, nxi[p]);
-                        float2 const dy = __fadd2_rn(by, nyi[p]);
-                        float2 const dz = __fadd2_rn(bz, nzi[p]);
-                        float2 r2 = __ffma2_rn(dz, dz, eps2);
-                        r2 = __ffma2_rn(dy, dy, r2);
-                        r2 = __ffma2_rn(dx, dx, r2);
-                        float2 const r6 = __fmul2_rn(__fmul2_rn(r2, r2), r2);
-                        float2 const inv = make_float2(rsqrtApprox(r6.x), rsqrtApprox(r6.y));
-                        float2 const s = __fmul2_rn(bm, inv);
-                        ax[p] = __ffma2_rn(s, dx, ax[p]);
-                        ay[p] = __ffma2_rn(s, dy, ay[p]);
-                        az[p] = __ffma2_rn(s, dz, az[p]);
+                        float4 const b = sj[t + q];
+                        float2 const bx = make_float2(b.x, b.x);
+                        float2 const by = make_float2(b.y, b.y);
+                        float2 const bz = make_float2(b.z, b.z);
+                        float2 const bm = make_float2(b.w, b.w);
+#pragma unroll
+                        for(int p = 0; p < PAIRS; ++p)
+                        {
+                            dx[q][p] = __fadd2_rn(bx, nxi[p]);
+                            dy[q][p] = __fadd2_rn(by, nyi[p]);
+                            dz[q][p] = __fadd2_rn(bz, nzi[p]);
+                            float2 r2 = __ffma2_rn(dz[q][p], dz[q][p], eps2);
+                            r2 = __ffma2_rn(dy[q][p], dy[q][p], r2);
+                            r2 = __ffma2_rn(dx[q][p], dx[q][p], r2);
+                            float2 const r6 = __fmul2_rn(__fmul2_rn(r2, r2), r2);
+                            float2 const inv = make_float2(rsqrtApprox(r6.x), rsqrtApprox(r6.y));
+                            sc[q][p] = __fmul2_rn(bm, inv);
+                        }
                     }
+#pragma unroll
+                    for(int q = 0; q < JILP; ++q)
+#pragma unroll
+                        for(int p = 0; p < PAIRS; ++p)
+                        {
+                            ax[p] = __ffma2_rn(sc[q][p], dx[q][p], ax[p]);
+                            ay[p] = __ffma2_rn(sc[q][p], dy[q][p], ay[p]);
+                            az[p] = __ffma2_rn(sc[q][p], dz[q][p], az[p]);
+                        }
                 }
             }
 
@@ -166,18 +180,22 @@ namespace a3b
         // 49.6, 2 x 128 40.2 (86% of the SMs' share filled), 3 x 128 36.0 (77%). The 64-thread shape is also the best
         // at the 32768 local bodies of 8 ranks (33.0 against 31.3).
         constexpr Shape kShapes[] = {
-            {1, 64, forceKickKernel<1, 64>},
-            {1, 128, forceKickKernel<1, 128>},
-            {2, 128, forceKickKernel<2, 128>},
-            {3, 128, forceKickKernel<3, 128>},
+            {1, 64, forceKickKernel<1, 64, 1>},
+            {1, 128, forceKickKernel<1, 128, 1>},
+            {2, 128, forceKickKernel<2, 128, 1>},
+            {3, 128, forceKickKernel<3, 128, 1>},
         };
+        // The 1 x 64 shape with the distance terms of two j-bodies evaluated side by side, for grids that leave at
+        // most 2 warps per SM sub-partition (local counts <= 65536): 32768 bodies 34.8 against 32.7 TFLOP/s, 65536
+        // 40.3 against 39.7; with more warps the plain loop is 0.5% faster (a four-j variant measured the same as two).
+        constexpr Shape kFewWarpsShape = {1, 64, forceKickKernel<1, 64, 2>};
         constexpr int kNumShapes = sizeof(kShapes) / sizeof(kShapes[0]);
 
         // Picks the shape whose blocks spread most evenly over the SMs: the busiest SM runs ceil(blocks / SMs)
         // blocks, so the useful fraction is iCount / (SMs * ceil(blocks / SMs) * bodies per block), scaled down when
         // an SM would hold fewer than 8 warps (too few to keep the FP32 pipe busy). Ties go to more pairs per
         // thread (more independent work per thread).
-        int pickShape(DeviceProps const* props, uint64_t iCount, int* shape)
+        int pickShape(DeviceProps const* props, uint64_t iCount, Shape const** shape)
         {
             static std::atomic<int> resident[kNumShapes][kMaxDevices] = {};
             double best = -1.0;
@@ -207,7 +225,11 @@ namespace a3b
 #ifdef A3B_NBODY_FORCE_SHAPE
             pick = A3B_NBODY_FORCE_SHAPE; // tuning builds: one fixed entry of kShapes
 #endif
-            *shape = pick;
+            *shape = &kShapes[pick];
+            uint64_t const perBlock0 = 2ull * kShapes[0].pairs * kShapes[0].threads;
+            uint64_t const perSm0 = ((iCount + perBlock0 - 1) / perBlock0 + props->smCount - 1) / props->smCount;
+            if(pick == 0 && perSm0 * (kShapes[0].threads / 32) <= 8)
+                *shape = &kFewWarpsShape; // <= 2 warps per sub-partition
             return A3B_OK;
         }
 
@@ -238,15 +260,15 @@ namespace a3b
             int rc = currentDevice(&props);
             if(rc)
                 return rc;
-            int k = 0;
-            rc = pickShape(props, iCount, &k);
+            Shape const* sh = nullptr;
+            rc = pickShape(props, iCount, &sh);
             if(rc)
                 return rc;
-            uint64_t const perBlock = 2ull * kShapes[k].pairs * kShapes[k].threads;
+            uint64_t const perBlock = 2ull * sh->pairs * sh->threads;
             uint64_t const blocks = (iCount + perBlock - 1) / perBlock;
             A3B_REQUIRE(blocks < 0x7FFFFFFFull, "problem too large");
-            kShapes[k].kernel<<<static_cast<unsigned>(blocks), kShapes[k].threads, 0, s>>>(m, x, y, z, nAll, iBegin,
-                                                                                           iCount, eps, dt, vx, vy, vz);
+            sh->kernel<<<static_cast<unsigned>(blocks), sh->threads, 0, s>>>(m, x, y, z, nAll, iBegin, iCount, eps, dt,
+                                                                             vx, vy, vz);
             A3B_CHECK_LAUNCH("nbody force launch");
             if(px)
             {
