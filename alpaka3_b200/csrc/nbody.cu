@@ -16,7 +16,8 @@
 // the 1e-4 tolerance; with the reference's order the kernel stays within 4e-6 (FMA contraction and the MUFU rsqrt
 // are the only differences). So the work is split over i only: a block owns 2 * PAIRS * THREADS i-bodies, walks
 // all j-bodies through shared memory tiles, and applies the kick v += a * dt to its own bodies at the end. The block
-// size is picked per launch so that the blocks spread evenly over the SMs.
+// size is picked per launch so that the blocks spread evenly over the SMs; grids that would leave 3-4 warps per SM
+// sub-partition run a variant with one i-body per thread and the j-bodies packed in pairs instead (same bits).
 #include "common.cuh"
 
 namespace a3b
@@ -147,6 +148,108 @@ namespace a3b
                 }
         }
 
+        // The same kick with one i-body per thread and the j-bodies taken in pairs: the distance terms of j and j+1
+        // are one packed FP32x2 operation each (the i-position broadcast into both halves once, before the loop), and
+        // the two contributions are accumulated one after the other, so every body still sums its j-bodies in index
+        // order with the same operations: the bits equal forceKickKernel's. Twice the threads of the packed-i kernel
+        // for the same bodies, at three more instructions per two pairs (scalar accumulation, a second 16-byte LDS):
+        // it wins where the packed-i grid leaves 3-4 warps per SM sub-partition (131072 local bodies: 45.9 against
+        // 43.0 TFLOP/s) and loses with more warps (262144: 47.7 against 50.2) or fewer (65536: 38.3 against 40.4).
+        template<int THREADS, int MINB>
+        __global__ void __launch_bounds__(THREADS, MINB) forceKickJPairKernel(
+            float const* __restrict__ m,
+            float const* __restrict__ x,
+            float const* __restrict__ y,
+            float const* __restrict__ z,
+            uint64_t nAll,
+            uint64_t iBegin,
+            uint64_t iCount,
+            float eps,
+            float dt,
+            float* __restrict__ vx,
+            float* __restrict__ vy,
+            float* __restrict__ vz)
+        {
+            constexpr int kJPairs = kJTile / 2;
+            __shared__ float4 sxy[kJPairs]; // {x_j, x_j+1, y_j, y_j+1}
+            __shared__ float4 szm[kJPairs]; // {z_j, z_j+1, m_j, m_j+1}
+            uint64_t const li = static_cast<uint64_t>(blockIdx.x) * THREADS + threadIdx.x;
+            bool const ok = li < iCount;
+            uint64_t const gi = iBegin + (ok ? li : 0u);
+            float const nx = ok ? -x[gi] : 0.f;
+            float const ny = ok ? -y[gi] : 0.f;
+            float const nz = ok ? -z[gi] : 0.f;
+            float2 const nx2 = make_float2(nx, nx);
+            float2 const ny2 = make_float2(ny, ny);
+            float2 const nz2 = make_float2(nz, nz);
+            float2 const eps2 = make_float2(eps, eps);
+            float ax = 0.f, ay = 0.f, az = 0.f;
+            for(uint64_t jt = 0; jt < nAll; jt += kJTile)
+            {
+                __syncthreads(); // the previous tile's readers are done
+                for(int p = threadIdx.x; p < kJPairs; p += THREADS)
+                {
+                    uint64_t const j0 = jt + 2 * p;
+                    uint64_t const j1 = j0 + 1;
+                    float4 a, b;
+                    if(j0 < nAll)
+                    {
+                        a.x = x[j0];
+                        a.z = y[j0];
+                        b.x = z[j0];
+                        b.z = m[j0];
+                    }
+                    else
+                    {
+                        a.x = a.z = b.x = kFar;
+                        b.z = 0.f;
+                    }
+                    if(j1 < nAll)
+                    {
+                        a.y = x[j1];
+                        a.w = y[j1];
+                        b.y = z[j1];
+                        b.w = m[j1];
+                    }
+                    else
+                    {
+                        a.y = a.w = b.y = kFar;
+                        b.w = 0.f;
+                    }
+                    sxy[p] = a;
+                    szm[p] = b;
+                }
+                __syncthreads();
+#pragma unroll 4
+                for(int p = 0; p < kJPairs; ++p)
+                {
+                    float4 const a = sxy[p];
+                    float4 const b = szm[p];
+                    float2 const dx = __fadd2_rn(make_float2(a.x, a.y), nx2);
+                    float2 const dy = __fadd2_rn(make_float2(a.z, a.w), ny2);
+                    float2 const dz = __fadd2_rn(make_float2(b.x, b.y), nz2);
+                    float2 r2 = __ffma2_rn(dz, dz, eps2);
+                    r2 = __ffma2_rn(dy, dy, r2);
+                    r2 = __ffma2_rn(dx, dx, r2);
+                    float2 const r6 = __fmul2_rn(__fmul2_rn(r2, r2), r2);
+                    float2 const inv = make_float2(rsqrtApprox(r6.x), rsqrtApprox(r6.y));
+                    float2 const sc = __fmul2_rn(make_float2(b.z, b.w), inv);
+                    ax = __fmaf_rn(sc.x, dx.x, ax);
+                    ay = __fmaf_rn(sc.x, dy.x, ay);
+                    az = __fmaf_rn(sc.x, dz.x, az);
+                    ax = __fmaf_rn(sc.y, dx.y, ax);
+                    ay = __fmaf_rn(sc.y, dy.y, ay);
+                    az = __fmaf_rn(sc.y, dz.y, az);
+                }
+            }
+            if(ok)
+            {
+                vx[li] = __fadd_rn(vx[li], __fmul_rn(ax, dt));
+                vy[li] = __fadd_rn(vy[li], __fmul_rn(ay, dt));
+                vz[li] = __fadd_rn(vz[li], __fmul_rn(az, dt));
+            }
+        }
+
         // drift x += v * dt of the local bodies (UpdatePositions, Kernels.hpp:126-142), after every kick of the step
         __global__ void __launch_bounds__(256) driftLocalKernel(
             float* __restrict__ x,
@@ -167,13 +270,18 @@ namespace a3b
             }
         }
 
-        // One block shape of the force kernel: its launch function and the resident blocks per SM.
+        // One block shape of the force kernel: i-bodies per thread (2 per packed pair, or 1 for the j-pair kernel),
+        // threads per block and its launch function.
         struct Shape
         {
             int pairs;
             int threads;
             void (*kernel)(float const*, float const*, float const*, float const*, uint64_t, uint64_t, uint64_t, float,
                            float, float*, float*, float*);
+            int bodiesPerThread() const
+            {
+                return pairs > 0 ? 2 * pairs : 1;
+            }
         };
 
         // Measured at 262144 bodies (B200, TFLOP/s by the 20-flop convention): 1 pair x 64 threads 50.2, 1 x 128
@@ -189,6 +297,9 @@ namespace a3b
         // most 2 warps per SM sub-partition (local counts <= 65536): 32768 bodies 34.8 against 32.7 TFLOP/s, 65536
         // 40.3 against 39.7; with more warps the plain loop is 0.5% faster (a four-j variant measured the same as two).
         constexpr Shape kFewWarpsShape = {1, 64, forceKickKernel<1, 64, 2>};
+        // One i-body per thread with j-bodies in pairs (forceKickJPairKernel), for grids of the 1 x 64 shape that
+        // leave 3-4 warps per SM sub-partition.
+        constexpr Shape kJPairShape = {0, 128, forceKickJPairKernel<128, 8>};
         constexpr int kNumShapes = sizeof(kShapes) / sizeof(kShapes[0]);
 
         // Picks the shape whose blocks spread most evenly over the SMs: the busiest SM runs ceil(blocks / SMs)
@@ -206,7 +317,7 @@ namespace a3b
                 int rc = residentPerSm(props, resident[k], kShapes[k].kernel, kShapes[k].threads, &r);
                 if(rc)
                     return rc;
-                uint64_t const perBlock = 2ull * kShapes[k].pairs * kShapes[k].threads;
+                uint64_t const perBlock = static_cast<uint64_t>(kShapes[k].bodiesPerThread()) * kShapes[k].threads;
                 uint64_t const blocks = (iCount + perBlock - 1) / perBlock;
                 uint64_t const sms = static_cast<uint64_t>(props->smCount);
                 uint64_t const perSm = (blocks + sms - 1) / sms;
@@ -226,10 +337,13 @@ namespace a3b
             pick = A3B_NBODY_FORCE_SHAPE; // tuning builds: one fixed entry of kShapes
 #endif
             *shape = &kShapes[pick];
-            uint64_t const perBlock0 = 2ull * kShapes[0].pairs * kShapes[0].threads;
+            uint64_t const perBlock0 = static_cast<uint64_t>(kShapes[0].bodiesPerThread()) * kShapes[0].threads;
             uint64_t const perSm0 = ((iCount + perBlock0 - 1) / perBlock0 + props->smCount - 1) / props->smCount;
-            if(pick == 0 && perSm0 * (kShapes[0].threads / 32) <= 8)
+            uint64_t const warps0 = perSm0 * (kShapes[0].threads / 32);
+            if(pick == 0 && warps0 <= 8)
                 *shape = &kFewWarpsShape; // <= 2 warps per sub-partition
+            else if(pick == 0 && warps0 <= 16)
+                *shape = &kJPairShape; // 3-4 warps per sub-partition
             return A3B_OK;
         }
 
@@ -264,7 +378,7 @@ namespace a3b
             rc = pickShape(props, iCount, &sh);
             if(rc)
                 return rc;
-            uint64_t const perBlock = 2ull * sh->pairs * sh->threads;
+            uint64_t const perBlock = static_cast<uint64_t>(sh->bodiesPerThread()) * sh->threads;
             uint64_t const blocks = (iCount + perBlock - 1) / perBlock;
             A3B_REQUIRE(blocks < 0x7FFFFFFFull, "problem too large");
             sh->kernel<<<static_cast<unsigned>(blocks), sh->threads, 0, s>>>(m, x, y, z, nAll, iBegin, iCount, eps, dt,

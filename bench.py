@@ -154,6 +154,8 @@ def time_steps(torch, dist_on, step, steps, warmup, kernel_events=True):
     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
     t0 = torch.cuda.Event(enable_timing=True)
     t1 = torch.cuda.Event(enable_timing=True)
+    if dist_on:
+        align_ranks(torch, s)
     t0.record(s)
     for k in range(steps):
         step(ev[k] if kernel_events else None)
@@ -165,6 +167,21 @@ def time_steps(torch, dist_on, step, steps, warmup, kernel_events=True):
     total = t0.elapsed_time(t1)
     kern = statistics.mean(a.elapsed_time(b) for a, b in ev) if kernel_events else None
     return total / steps, kern
+
+
+ALIGN_SPIN_CYCLES = 4_000_000  # ~2 ms at 1.965 GHz
+
+
+def align_ranks(torch, s):
+    """Untimed device-side start line of a timed region on several ranks. The host processes leave the barrier tens
+    of microseconds apart, and the ranks' timed kernels wait for one another (peer exchanges, NCCL), so without this
+    every rank's first event would include the slowest host's lag. Each rank's stream first spins ~2 ms on its GPU
+    (long enough for the host to queue the timed steps behind it), then passes a one-element all-reduce, which the
+    ranks' streams leave within a few microseconds of each other; the start event is recorded right after it."""
+    import torch.distributed as dist
+    torch.cuda._sleep(ALIGN_SPIN_CYCLES)
+    t = torch.zeros(1, device=s.device)
+    dist.all_reduce(t)
 
 
 def max_over_ranks(torch, dist_on, v):

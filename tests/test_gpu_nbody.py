@@ -70,10 +70,12 @@ def test_nbody_split_i_range_matches_whole(cuda, port):
         assert torch.equal(a, b)
 
 
-def test_nbody_large_ragged_i_range_matches_slices(cuda, port):
+@pytest.mark.parametrize("slice_len", [40000, 120000])
+def test_nbody_large_ragged_i_range_matches_slices(cuda, port, slice_len):
     """A kick over 263181 bodies (ragged: neither a multiple of the j-tile nor of the block's group) equals the kicks
-    over slices of 40000 bodies (other grids, the few-warps variant among them): every body sums its j-bodies in
-    index order whatever the launch shape, so the bits agree; two kicks in a row accumulate the same way."""
+    over slices of 40000 bodies (the few-warps variant of the packed-i kernel) or 120000 bodies (the j-pair kernel):
+    every body sums its j-bodies in index order whatever the launch shape, so the bits agree; two kicks in a row
+    accumulate the same way."""
     from alpaka3_b200 import algo
     n = 262144 + 1000 + 37
     m = _t(port.gen_f32(n, 0.5, 1.0, seed=31), cuda)
@@ -83,8 +85,8 @@ def test_nbody_large_ragged_i_range_matches_slices(cuda, port):
         algo.nbody_update_velocities(m, x, y, z, *va, 1e-3, 1e-3)
     vb = [torch.zeros(n, dtype=torch.float32, device=cuda) for _ in range(3)]
     for _ in range(2):
-        for b in range(0, n, 40000):
-            e = min(n, b + 40000)
+        for b in range(0, n, slice_len):
+            e = min(n, b + slice_len)
             algo.nbody_update_velocities(m, x, y, z, *(v[b:e] for v in vb), 1e-3, 1e-3, i_begin=b)
     torch.cuda.synchronize()
     from alpaka3_b200 import capi
