@@ -9,9 +9,12 @@ peer's mapped slot buffer over NVLink and combines the world's partials in rank 
 `--collective nccl` uses an NCCL all-reduce after the kernel instead, and the fused run also reports that variant's
 time). `value` is the whole-job throughput (4 * 2^30 bytes per step / max-over-ranks step time) with the inputs
 resident in HBM; `e2e` is the same step through the C ABI from pinned HOST memory (host->device copy of each rank's
-shard and device->host read of the result inside the timed region). At N = 1 the line also carries `parts`: the other
-kernels the metric names (BabelStream triad and dot at 2^25 fp64, exclusive scan of 2^30 int32, inclusive scan of
-2^28 uint64), each device-timed the same way. The inputs (>= 268 MB per array) exceed the 126 MB L2 in every case.
+shard and device->host read of the result inside the timed region). The line also carries `parts`: the other
+kernels the metric names (BabelStream copy/mul/add/triad and dot at 2^25 fp64, exclusive scan of 2^30 int32,
+inclusive scan of 2^28 uint64, nBody, heat, HACCmk), each device-timed the same way, on one GPU at N = 1 and sharded
+over the same ranks at N > 1, and a `parity` block (small-size checks of every sharded path). On several ranks every
+timed region starts at a device-side start line (align_ranks), after the host barrier. The inputs (>= 268 MB per
+array) exceed the 126 MB L2 in every case.
 
 `--impl reference` times alpaka3's own OpenMP host backend (oracle/_ref, compiled from the reference headers) on the
 host cores for the same metric and workload; under torchrun only rank 0 runs it.
@@ -339,7 +342,11 @@ def run_b200(args):
             "roofline": {"bound": "hbm", "achieved": round(kern_gbs, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(kern_gbs / peak, 4), "peak_kind": peak_kind,
                          "traffic": SUMSQ_TRAFFIC_PER_LAUNCH(n_local),
-                         "kernel": "reduceKernel<float, 8 per pack, plus, square> (a3b_transform_reduce)",
+                         "kernel": ("reduceAllRanksKernel<float, 8 per pack, plus, square> "
+                                    "(a3b_transform_reduce_allranks)" if group is not None else
+                                    "reduceKernel<float, 8 per pack, plus, square> (a3b_transform_reduce_partial)"
+                                    if dist_on else
+                                    "reduceKernel<float, 8 per pack, plus, square> (a3b_transform_reduce)"),
                          "kernel_ms": round(kern_ms, 5)},
             "e2e": e2e, "gpu_launches": launches[0], "clocks": sampler.summary(),
         }
