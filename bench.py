@@ -182,7 +182,9 @@ def align_ranks(torch, s):
     (long enough for the host to queue the timed steps behind it), then passes a one-element all-reduce, which the
     ranks' streams leave within a few microseconds of each other; the start event is recorded right after it."""
     import torch.distributed as dist
-    torch.cuda._sleep(ALIGN_SPIN_CYCLES)
+    spin = getattr(torch.cuda, "_sleep", None)  # torch's clock-spin kernel; without it only the all-reduce aligns
+    if spin is not None:
+        spin(ALIGN_SPIN_CYCLES)
     t = torch.zeros(1, device=s.device)
     dist.all_reduce(t)
 
