@@ -37,10 +37,10 @@ namespace a3b
             return r;
         }
 
-        // At least 8 resident blocks: measured 50.2 TFLOP/s (64 threads) against 45.9 without the bound at 262144
+        // At least MINB resident blocks: with 8, 50.2 TFLOP/s (64 threads) against 45.9 without the bound at 262144
         // bodies; the compiler keeps more j-steps in flight.
-        template<int PAIRS, int THREADS, int JILP>
-        __global__ void __launch_bounds__(THREADS, 8) forceKickKernel(
+        template<int PAIRS, int THREADS, int JILP, int MINB>
+        __global__ void __launch_bounds__(THREADS, MINB) forceKickKernel(
             float const* __restrict__ m,
             float const* __restrict__ x,
             float const* __restrict__ y,
@@ -286,17 +286,19 @@ namespace a3b
 
         // Measured at 262144 bodies (B200, TFLOP/s by the 20-flop convention): 1 pair x 64 threads 50.2, 1 x 128
         // 49.6, 2 x 128 40.2 (86% of the SMs' share filled), 3 x 128 36.0 (77%). The 64-thread shape is also the best
-        // at the 32768 local bodies of 8 ranks (33.0 against 31.3).
+        // at the 32768 local bodies of 8 ranks (33.0 against 31.3). Its entry evaluates the distance terms of two
+        // j-bodies side by side under a register cap for 10 resident blocks (5 warps per SM sub-partition): 50.6
+        // against 50.1 for the plain loop at 8 blocks, measured in the same process.
         constexpr Shape kShapes[] = {
-            {1, 64, forceKickKernel<1, 64, 1>},
-            {1, 128, forceKickKernel<1, 128, 1>},
-            {2, 128, forceKickKernel<2, 128, 1>},
-            {3, 128, forceKickKernel<3, 128, 1>},
+            {1, 64, forceKickKernel<1, 64, 2, 10>},
+            {1, 128, forceKickKernel<1, 128, 1, 8>},
+            {2, 128, forceKickKernel<2, 128, 1, 8>},
+            {3, 128, forceKickKernel<3, 128, 1, 8>},
         };
         // The 1 x 64 shape with the distance terms of two j-bodies evaluated side by side, for grids that leave at
         // most 2 warps per SM sub-partition (local counts <= 65536): 32768 bodies 34.8 against 32.7 TFLOP/s, 65536
-        // 40.3 against 39.7; with more warps the plain loop is 0.5% faster (a four-j variant measured the same as two).
-        constexpr Shape kFewWarpsShape = {1, 64, forceKickKernel<1, 64, 2>};
+        // 40.3 against 39.7 (a four-j variant measured the same as two).
+        constexpr Shape kFewWarpsShape = {1, 64, forceKickKernel<1, 64, 2, 8>};
         // One i-body per thread with j-bodies in pairs (forceKickJPairKernel), for grids of the 1 x 64 shape that
         // leave 3-4 warps per SM sub-partition.
         constexpr Shape kJPairShape = {0, 128, forceKickJPairKernel<128, 8>};
