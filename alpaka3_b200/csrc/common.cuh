@@ -61,12 +61,6 @@ namespace a3b
     // properties of the current device (cached); returns A3B_OK or an error status
     int currentDevice(DeviceProps const** props);
 
-    // A fully ordered launch on (device ordinal, stream) of a kernel that signals its dependents
-    // (griddepcontrol.launch_dependents) before it has written all of [out, out + outBytes): a reduction launched next
-    // with the early start could start while that output is still being written, so the reductions' early-start
-    // guard (reduce.cu) records it like the output of an early-started reduction.
-    void noteEarlySignalingLaunch(int dev, cudaStream_t s, void const* out, uint64_t outBytes);
-
     // device ordinals the library serves (0 .. kMaxDevices-1)
     constexpr int kMaxDevices = 64;
 

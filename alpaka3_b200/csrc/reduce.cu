@@ -560,8 +560,6 @@ namespace a3b
         std::set<std::pair<int, cudaStream_t>> gEarlyEnabled;
         std::map<std::pair<int, cudaStream_t>, std::vector<std::pair<uintptr_t, uintptr_t>>> gEarlyOutputs;
 
-        // Disabling keeps the history: a scan (which signals its dependents before it ends, noteEarlySignalingLaunch)
-        // may still be writing an output when the early start is enabled again before the next reduction.
         void setEarlyStart(int dev, cudaStream_t s, bool enable)
         {
             std::lock_guard<std::mutex> lock(gEarlyMutex);
@@ -569,7 +567,10 @@ namespace a3b
             if(enable)
                 gEarlyEnabled.insert(key);
             else
+            {
                 gEarlyEnabled.erase(key);
+                gEarlyOutputs.erase(key);
+            }
         }
 
         // true: launch with the early start; in both cases `out` (8 bytes) joins the stream's history
@@ -1083,15 +1084,6 @@ namespace a3b
             }
         }
     } // namespace
-
-    void noteEarlySignalingLaunch(int dev, cudaStream_t s, void const* out, uint64_t outBytes)
-    {
-        std::lock_guard<std::mutex> lock(gEarlyMutex);
-        auto& h = gEarlyOutputs[std::make_pair(dev, s)];
-        h.clear(); // the launch is fully ordered: every earlier kernel of the stream has completed when it starts
-        auto const o = reinterpret_cast<uintptr_t>(out);
-        h.emplace_back(o, o + outBytes);
-    }
 } // namespace a3b
 
 namespace a3b

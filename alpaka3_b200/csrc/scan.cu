@@ -269,10 +269,6 @@ namespace a3b
             bool abort = false;
             for(int64_t i = -L; i <= lastRound; ++i)
             {
-                // entering its last round, the block lets a reduction launched next with the early start begin
-                // (launchScan records the output for the reductions' early-start guard)
-                if(i == lastRound && threadIdx.x == 0)
-                    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
                 if(VEC && threadIdx.x == 0)
                 {
                     bulkWaitRead<1>(); // the slot refilled now was stored two rounds ago
@@ -539,8 +535,6 @@ namespace a3b
                 args,
                 dyn,
                 s));
-            // the blocks signal their dependents in their last round, while they still write `out`
-            noteEarlySignalingLaunch(props->ordinal, s, out, n * sizeof(T));
             return A3B_OK;
         }
 

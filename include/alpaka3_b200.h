@@ -196,11 +196,9 @@ A3B_API int a3b_transform_reduce_noalloc(a3b_stream_t stream, int dtype, int red
  * complete only before it touches its scratch or `out`. The next call thus streams its input while this one combines
  * (and, across ranks, waits for its peers). The library launches fully ordered any call whose input overlaps the
  * output of one of its own reductions that may still run (every reduction started early since the last fully ordered
- * launch). The library's scans signal their dependents in their last round (a reduction after a scan may start
- * while the scan finishes); their outputs are tracked the same way. ENABLE IT ONLY IF no other kernel on the stream
- * executes griddepcontrol.launch_dependents (cudaTriggerProgrammaticLaunchCompletion) before its output is written --
- * e.g. kernels built with programmatic dependent launch by CUTLASS or some cuBLASLt kernels: the reduction could read
- * that output before it is written.
+ * launch). ENABLE IT ONLY IF no other kernel on the stream executes griddepcontrol.launch_dependents
+ * (cudaTriggerProgrammaticLaunchCompletion) before its output is written -- e.g. kernels built with programmatic
+ * dependent launch by CUTLASS or some cuBLASLt kernels: the reduction could read that output before it is written.
  * Copies, memsets and kernels without that instruction are always complete before the reduction reads its input. */
 A3B_API int a3b_set_early_start(a3b_stream_t stream, int enable);
 
