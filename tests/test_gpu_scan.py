@@ -200,3 +200,37 @@ def test_float_scan_is_deterministic(cuda):
         for _ in range(3):
             algo.inclusive_scan(b, x)
             assert torch.equal(a, b)
+
+
+def test_early_started_reduce_after_scan(cuda):
+    """Reductions with the early start enabled right after a scan on the same stream: one of the scan's output (out of
+    place or in place) must see every element the scan wrote, one of the scan's input stays correct. int32 sums wrap,
+    so the checks are bit-exact."""
+    from alpaka3_b200 import algo
+    n = (1 << 26) + 5
+    x = torch.empty(n, dtype=torch.int32, device=cuda)
+    algo.random_u32(x, 0x5EED, shift=28)
+    xl = x.long()
+    excl = torch.cumsum(xl, 0) - xl
+    want_scan = int(((excl.sum() + (1 << 31)) % (1 << 32)) - (1 << 31))
+    want_x = int(((xl.sum() + (1 << 31)) % (1 << 32)) - (1 << 31))
+    del xl, excl
+    y = torch.empty_like(x)
+    z = torch.empty_like(x)
+    s1, s2, s3 = (torch.empty(1, dtype=torch.int32, device=cuda) for _ in range(3))
+    algo.set_early_start(True)
+    try:
+        for _ in range(4):
+            algo.exclusive_scan(y, x)               # out of place
+            algo.reduce(None, s1, "plus", y)        # reads the scan's output
+            z.copy_(x)
+            algo.exclusive_scan(z, z)               # in place
+            algo.reduce(None, s2, "plus", z)        # reads the in-place output
+            algo.exclusive_scan(y, x)
+            algo.reduce(None, s3, "plus", x)        # the scan's input
+            torch.cuda.synchronize()
+            assert int(s1.item()) == want_scan
+            assert int(s2.item()) == want_scan
+            assert int(s3.item()) == want_x
+    finally:
+        algo.set_early_start(False)
